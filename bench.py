@@ -1,0 +1,551 @@
+"""
+Benchmark of the paged-KV hot path on B200: paged decode attention over all 16
+layers of Llama-3.2-1B geometry at batch 256.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+A step = one decode step of the hot path: for each of the 16 layers, the
+KV-append of one new token per sequence (append_kv) then paged attention over
+the full history (attend). Workload (seeded, synthetic — the reference uses no
+dataset on this path): 256 sequences with context lengths lognormal(mu =
+ln 256 - 0.32, sigma = 0.8) clipped to [1, 2048] (mean ~258, p90 ~524); 16-token
+blocks scattered over a pool of 90% of HBM by a seeded permutation; K, V ~ N(0,
+0.5) fp16 (variance 0.5), Q ~ N(0, 1). Sequences grow by one token per step.
+
+Output: ONE JSON line on rank 0. ``value`` = aggregate tok/s with inputs resident
+in HBM (per-step CUDA graphs replayed back to back; each step reads ~2.2 GB of
+KV, far larger than L2, so no flush is needed); ``e2e`` = the same metric
+through the public Python API with host buffers and per-step H2D/D2H inside
+the timed region; ``roofline`` = the decode kernel's algorithmic bytes per
+launch / its CUDA-event-timed average launch duration vs measured HBM peak;
+``cpu_baseline`` = the CPU oracle (the reference algorithm restated) on this
+host. Multi-GPU (torchrun): independent replicas, no data-path collective.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+L, HKV, HQ, D, P = 16, 8, 32, 64, 16
+N_SEQ = 256
+SCALE = 1.0 / 8.0
+KV_STD = math.sqrt(0.5)
+METRIC = "paged decode-attn tok/s/GPU & HBM GB/s %peak; KV swap GB/s; at 1/2/4/8 GPU"
+UNIT = "tok/s"
+WORKLOAD = ("config2: fp16 paged decode attention + KV-append, 16 layers, batch 256, "
+            "Llama-3.2-1B GQA 32q/8kv/d64, 16-token blocks, lognormal ctx mean~258 p90~524 cap 2048, "
+            "pool 90% of HBM scattered by seeded permutation")
+
+
+def contexts(rs: np.random.RandomState, n: int = N_SEQ) -> np.ndarray:
+    """Reference's length distribution (bench/capacity.py:236,303-305)."""
+    return np.clip(np.round(rs.lognormal(math.log(256) - 0.32, 0.8, size=n)), 1, 2048).astype(np.int64)
+
+
+# ------------------------------------------------------------------ helpers
+
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id: str):
+        self.gpu_id = gpu_id
+        self.proc = None
+        self.f = None
+
+    def start(self):
+        try:
+            self.f = tempfile.TemporaryFile(mode="w+")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", self.gpu_id, f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "50"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self) -> dict | None:
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.f.seek(0)
+        rows = [r.split(",") for r in self.f.read().strip().splitlines() if r.strip()]
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            r = [x.strip() for x in r]
+            if len(r) < 9:
+                continue
+            try:
+                sm.append(float(r[1]))
+                mx.append(float(r[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, r[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def measured_peaks() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    try:
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def cpu_threads() -> int:
+    try:
+        import threadpoolctl
+        info = threadpoolctl.threadpool_info()
+        n = [i.get("num_threads", 0) for i in info if i.get("user_api") == "blas"]
+        if n:
+            return int(max(n))
+    except Exception:
+        pass
+    return os.cpu_count() or 1
+
+
+# ------------------------------------------------------------------ CPU oracle timing
+
+
+def cpu_oracle_step_time(seed: int, budget_s: float = 10.0) -> dict:
+    """Time the CPU oracle (the reference's append_kv + attend restated in numpy,
+    float32 — CPU half-precision matmul has no BLAS path) on one layer of the
+    full 256-sequence batch, repeated for ~budget_s; returns seconds per layer."""
+    from oracle import OraclePool, attend_reference  # CPU baseline leg only
+    from llm_serving_layer_b200.meta import build_meta
+
+    rs = np.random.RandomState(seed)
+    ctx = contexts(rs)
+    pages = (ctx + P - 1) // P
+    nb = int(pages.sum())
+    perm = rs.permutation(nb)
+    tables, o = [], 0
+    for p in pages:
+        tables.append(perm[o:o + p].tolist())
+        o += p
+    pool = OraclePool(1, nb, P, HKV, D, dtype=np.float32)
+    pool.k[0][:] = (rs.standard_normal(pool.k[0].shape) * KV_STD).astype(np.float32)
+    pool.v[0][:] = (rs.standard_normal(pool.v[0].shape) * KV_STD).astype(np.float32)
+    m = build_meta(tables, ctx, [1] * N_SEQ, P)
+    slots = m.slot_mapping.numpy()
+    q = rs.standard_normal((N_SEQ, HQ, D)).astype(np.float32)
+    kn = (rs.standard_normal((N_SEQ, HKV, D)) * KV_STD).astype(np.float32)
+    vn = (rs.standard_normal((N_SEQ, HKV, D)) * KV_STD).astype(np.float32)
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while True:
+        t0 = time.perf_counter()
+        pool.append_kv(0, kn, vn, slots)
+        attend_reference(q, pool.k[0], pool.v[0], SCALE, m)
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() > t_end and len(times) >= 2:
+            break
+    per_layer = statistics.median(times)
+    return {"per_layer_s": per_layer, "iters": len(times), "cores": cpu_threads(),
+            "sum_ctx": int(ctx.sum())}
+
+
+# ------------------------------------------------------------------ reference arm
+
+
+def run_reference(args) -> None:
+    ws, rank, _ = dist_env()
+    if rank != 0:
+        return
+    steps, warmup = args.steps_ref, args.warmup
+    from oracle import OraclePool, attend_reference  # the reference arm times the oracle port
+    from llm_serving_layer_b200.meta import build_meta
+
+    rs = np.random.RandomState(args.seed)
+    ctx = contexts(rs)
+    pages = (ctx + steps + warmup + P - 1) // P
+    nb = int(pages.sum())
+    perm = rs.permutation(nb)
+    tables, o = [], 0
+    for p in pages:
+        tables.append(perm[o:o + p].tolist())
+        o += p
+    pool = OraclePool(1, nb, P, HKV, D, dtype=np.float32)
+    pool.k[0][:] = (rs.standard_normal(pool.k[0].shape) * KV_STD).astype(np.float32)
+    pool.v[0][:] = (rs.standard_normal(pool.v[0].shape) * KV_STD).astype(np.float32)
+    q = rs.standard_normal((N_SEQ, HQ, D)).astype(np.float32)
+    kn = (rs.standard_normal((N_SEQ, HKV, D)) * KV_STD).astype(np.float32)
+    vn = (rs.standard_normal((N_SEQ, HKV, D)) * KV_STD).astype(np.float32)
+    times = []
+    for s in range(warmup + steps):
+        m = build_meta(tables, ctx + s, [1] * N_SEQ, P)
+        t0 = time.perf_counter()
+        pool.append_kv(0, kn, vn, m.slot_mapping.numpy())
+        attend_reference(q, pool.k[0], pool.v[0], SCALE, m)
+        dt = time.perf_counter() - t0
+        if s >= warmup:
+            times.append(dt)
+    per_layer = sum(times) / len(times)
+    step_s = per_layer * L  # one sampled layer per step, scaled to the 16-layer step
+    value = N_SEQ / step_s
+    cores = cpu_threads()
+    sample = (f"each step: 1 of the 16 layers (append_kv + attend) over the full 256-sequence batch, "
+              f"float32 numpy port of PagedTorchBackend on {cores} BLAS threads; tok/s scaled to 16 layers")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": UNIT,
+        "n_gpus": ws, "steps": steps, "warmup": warmup, "ms_per_step": round(step_s * 1e3, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": {"workload": WORKLOAD, "global_batch": N_SEQ * ws, "seq_len": 2048},
+        "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ B200 arm
+
+
+def build_workload(torch, bk, rs, steps_total, device):
+    """Scattered tables with room for every step, history K/V filled on device."""
+    from llm_serving_layer_b200.meta import build_meta
+
+    ctx = contexts(rs)
+    pages = (ctx + steps_total + P - 1) // P
+    total = int(pages.sum())
+    perm = torch.from_numpy(rs.permutation(bk.num_blocks)[:total].astype(np.int64))
+    tables, o = [], 0
+    for p in pages:
+        tables.append(perm[o:o + p].tolist())
+        o += p
+    idx = perm.to(device)
+    g = torch.Generator(device=device).manual_seed(int(rs.randint(1 << 30)))
+    for layer in range(L):
+        for kv in range(2):
+            vals = torch.randn((total, P, HKV, D), generator=g, device=device) * KV_STD
+            bk._pool[layer, kv].index_copy_(0, idx, vals.to(bk.dtype))
+            del vals
+    metas = [build_meta(tables, ctx + s, [1] * N_SEQ, P, device=device) for s in range(steps_total)]
+    return ctx, tables, metas
+
+
+def run_b200(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    from llm_serving_layer_b200 import B200PagedBackend, B200SwapSpace
+    from llm_serving_layer_b200.meta import build_meta
+
+    ws, rank, local = dist_env()
+    if ws > 1:
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    seed = args.seed + 1000 * rank
+    rs = np.random.RandomState(seed)
+
+    free, total_mem = torch.cuda.mem_get_info(device)
+    block_bytes = B200PagedBackend.estimate_pool_bytes(L, 1, P, HKV, D, torch.float16)
+    pool_bytes = min(int(args.pool_frac * total_mem), free - (8 << 30))
+    num_blocks = max(1024, pool_bytes // block_bytes)
+    bk = B200PagedBackend(L, num_blocks, P, HKV, HQ, D, device=device, dtype=torch.float16, validate="device")
+
+    n_graphs = min(args.steps, args.max_graphs)
+    steps_total = args.warmup + n_graphs
+    ctx, tables, metas = build_workload(torch, bk, rs, steps_total, device)
+    g = torch.Generator(device=device).manual_seed(seed)
+    qs = [torch.randn((N_SEQ, HQ, D), generator=g, device=device).half() for _ in range(L)]
+    ks = [(torch.randn((N_SEQ, HKV, D), generator=g, device=device) * KV_STD).half() for _ in range(L)]
+    vs = [(torch.randn((N_SEQ, HKV, D), generator=g, device=device) * KV_STD).half() for _ in range(L)]
+    bk.reserve_workspace(N_SEQ, max(int(m.kv_indices.shape[0]) for m in metas))
+
+    def step_eager(m):
+        bk.plan(m)
+        outs = []
+        for layer in range(L):
+            bk.append_kv(layer, ks[layer], vs[layer], m)
+            outs.append(bk.attend(qs[layer], layer, SCALE, m))
+        return outs
+
+    # warm every cache (tensor maps, occupancy, allocator) eagerly, then capture
+    for m in metas[: args.warmup]:
+        step_eager(m)
+    torch.cuda.synchronize()
+    bk.check_status()
+
+    graphs, ev = [], []
+    pool_handle = None
+    for m in metas[args.warmup:]:
+        bk.invalidate_plan()
+        gr = torch.cuda.CUDAGraph()
+        evs = [(torch.cuda.Event(enable_timing=True, external=True),
+                torch.cuda.Event(enable_timing=True, external=True)) for _ in range(L)]
+        with torch.cuda.graph(gr, pool=pool_handle):
+            bk.plan(m)
+            for layer in range(L):
+                bk.append_kv(layer, ks[layer], vs[layer], m)
+                evs[layer][0].record()
+                bk.attend(qs[layer], layer, SCALE, m)
+                evs[layer][1].record()
+        pool_handle = gr.pool()
+        graphs.append(gr)
+        ev.append(evs)
+    for gr in graphs[: min(len(graphs), 3)]:  # graph warm-up
+        gr.replay()
+    torch.cuda.synchronize()
+
+    # ---- timed region: K steps (the captured steps replayed in order, cycling)
+    gpu_id = str(local)
+    try:
+        uuid = torch.cuda.get_device_properties(device).uuid
+        gpu_id = f"GPU-{uuid}" if not str(uuid).startswith("GPU-") else str(uuid)
+    except Exception:
+        pass
+    clocks = ClockSampler(gpu_id)
+    if ws > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    time.sleep(0.05)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for s in range(args.steps):
+        graphs[s % n_graphs].replay()
+    e1.record()
+    torch.cuda.synchronize()
+    clock_info = clocks.stop()
+    ms = e0.elapsed_time(e1)
+    if ws > 1:
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.barrier()
+        ms = float(t.item())
+    bk.check_status()
+    ms_per_step = ms / args.steps
+    value = N_SEQ * ws * args.steps / (ms / 1e3)
+
+    # ---- roofline of the decode kernel (its launches inside the graphs)
+    dur = [ev[s][l][0].elapsed_time(ev[s][l][1]) for s in range(n_graphs) for l in range(L)]
+    avg_launch_ms = sum(dur) / len(dur)
+    alg = []
+    for m in metas[args.warmup:]:
+        kv = m.kv_lens.sum().item()
+        pages_m = int(m.kv_indices.shape[0])
+        # K+V read of every token's row, Q read + O write, one 8-byte page descriptor per page
+        alg.append(kv * HKV * D * 2 * 2 + N_SEQ * HQ * D * 2 * 2 + pages_m * 8)
+    alg_bytes = sum(alg) / len(alg)
+    peak, peak_kind = measured_peaks()
+    achieved = alg_bytes / (avg_launch_ms / 1e3) / 1e9
+    traffic = None
+    tfile = ROOT / "profiles" / "decode_traffic.json"
+    if tfile.exists():
+        try:
+            tj = json.loads(tfile.read_text())
+            traffic = round(float(tj["dram_bytes_per_alg_byte"]) * alg_bytes)
+        except Exception:
+            traffic = None
+
+    # ---- e2e: public API, host buffers, H2D + D2H inside the timed region
+    e2e = run_e2e(torch, bk, tables, ctx, args, device, ws, dist, n_graphs)
+
+    line_extra = {}
+    # ---- swap (config 4), rank 0 measures its own GPU's host link
+    if args.swap and rank == 0:
+        line_extra["swap"] = run_swap(torch, bk, args, device)
+    if ws > 1:
+        dist.barrier()
+
+    if rank == 0:
+        cpu = cpu_oracle_step_time(args.seed, args.cpu_budget) if args.cpu_budget > 0 else None
+        cpu_line = None
+        if cpu:
+            cpu_line = {"value": round(N_SEQ / (cpu["per_layer_s"] * L), 3), "unit": UNIT, "cores": cpu["cores"],
+                        "kind": "port",
+                        "sample": (f"{cpu['iters']} repetitions of one layer (append_kv + attend) over the full "
+                                   f"256-sequence batch (sum ctx {cpu['sum_ctx']}), float32 numpy restatement of "
+                                   "PagedTorchBackend; tok/s scaled to a 16-layer step")}
+        line = {
+            "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "global_batch": N_SEQ * ws, "seq_len": 2048,
+                       "parallelism": f"replicas{ws}", "num_blocks": int(num_blocks),
+                       "pool_gb": round(bk.pool_bytes() / 1e9, 1), "distinct_steps": n_graphs,
+                       "l2": "inputs larger than L2 (~2.2 GB of KV read per step)"},
+            "e2e": e2e,
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": traffic,
+                         "peak_kind": peak_kind, "kernel": "decode_kernel",
+                         "alg_bytes_per_launch": int(alg_bytes), "avg_launch_us": round(avg_launch_ms * 1e3, 2)},
+            "cpu_baseline": cpu_line,
+            "gpu_launches": args.steps * (1 + 2 * L),
+            "clocks": clock_info,
+            **line_extra,
+        }
+        print(json.dumps(line), flush=True)
+    del graphs
+    if ws > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_e2e(torch, bk, tables, ctx, args, device, ws, dist, n_graphs) -> dict:
+    """Public-API end to end: per step, build the BatchMeta on the host, copy it
+    and the step's q/k/v (16 layers) from pinned host memory, run append_kv +
+    attend per layer, copy every layer's attention output back to pinned host
+    memory, synchronise. Timed with CUDA events around the whole loop."""
+    from llm_serving_layer_b200.meta import build_meta
+
+    steps = args.e2e_steps
+    base = args.warmup  # fresh lengths continue from the graph steps' start
+    rs = np.random.RandomState(args.seed + 7)
+    hq = [torch.from_numpy(rs.standard_normal((N_SEQ, HQ, D)).astype(np.float16)).pin_memory() for _ in range(L)]
+    hk = [torch.from_numpy((rs.standard_normal((N_SEQ, HKV, D)) * KV_STD).astype(np.float16)).pin_memory()
+          for _ in range(L)]
+    hv = [torch.from_numpy((rs.standard_normal((N_SEQ, HKV, D)) * KV_STD).astype(np.float16)).pin_memory()
+          for _ in range(L)]
+    hout = [torch.empty((N_SEQ, HQ, D), dtype=torch.float16).pin_memory() for _ in range(L)]
+    dq = [torch.empty_like(x, device=device) for x in hq]
+    dk = [torch.empty_like(x, device=device) for x in hk]
+    dv = [torch.empty_like(x, device=device) for x in hv]
+    meta_bytes = 0
+
+    def one(s):
+        nonlocal meta_bytes
+        m = build_meta(tables, ctx + base + (s % n_graphs), [1] * N_SEQ, P, device=device, pin=True)
+        meta_bytes = sum(int(getattr(m, f).numel() * getattr(m, f).element_size()) for f in (
+            "query_lens", "cu_query_lens", "kv_lens", "positions", "last_token_ix", "kv_indptr",
+            "kv_indices", "kv_last_page_len", "batch_indices", "slot_mapping"))
+        for layer in range(L):
+            dq[layer].copy_(hq[layer], non_blocking=True)
+            dk[layer].copy_(hk[layer], non_blocking=True)
+            dv[layer].copy_(hv[layer], non_blocking=True)
+            bk.append_kv(layer, dk[layer], dv[layer], m)
+            o = bk.attend(dq[layer], layer, SCALE, m)
+            hout[layer].copy_(o, non_blocking=True)
+        torch.cuda.current_stream(device).synchronize()
+
+    for s in range(3):
+        one(s)
+    if ws > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for s in range(steps):
+        one(s)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    if ws > 1:
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    bk.check_status()
+    h2d = L * (hq[0].numel() + hk[0].numel() + hv[0].numel()) * 2 + meta_bytes
+    d2h = L * hout[0].numel() * 2
+    return {"value": round(N_SEQ * ws * steps / (ms / 1e3), 1), "unit": UNIT, "h2d_bytes_per_step": int(h2d),
+            "d2h_bytes_per_step": int(d2h), "steps": steps, "ms_per_step": round(ms / steps, 4),
+            "path": "B200PagedBackend.append_kv/attend per layer, validate='device', host BatchMeta built per step"}
+
+
+def run_swap(torch, bk, args, device) -> dict:
+    """Config 4: 64 victims x 1024 tokens (64 blocks each, scattered), swap-out to
+    pinned host and swap-in to fresh blocks, bit-exact check, alone and with a
+    concurrent batch-128 decode on the compute stream."""
+    from llm_serving_layer_b200 import B200SwapSpace
+
+    class Blocks:  # the block-manager view the swap space reads
+        def __init__(self, ids, n):
+            self.block_ids, self.num_tokens, self.seq_id, self.is_freed = list(ids), n, 0, False
+
+    rs = np.random.RandomState(args.seed + 4)
+    victims, toks = 64, 1024
+    nbv = toks // P
+    perm = rs.permutation(bk.num_blocks)
+    src = [perm[i * nbv:(i + 1) * nbv].tolist() for i in range(victims)]
+    dst = [perm[(victims + i) * nbv:(victims + i + 1) * nbv].tolist() for i in range(victims)]
+    sw = B200SwapSpace(bk, staging_bytes=256 << 20, synchronous=False)
+    per_dir = victims * sw.bytes_for(nbv)
+
+    def once():
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        hs = [sw.swap_out(f"v{i}", Blocks(src[i], toks)) for i in range(victims)]
+        sw.wait()
+        t1 = time.perf_counter()
+        for i, h in enumerate(hs):
+            sw.swap_in(h, Blocks(dst[i], toks))
+        sw.wait()
+        torch.cuda.synchronize()
+        t2 = time.perf_counter()
+        return hs, t1 - t0, t2 - t1
+
+    hs, _, _ = once()
+    for h in hs:
+        sw.release(h)
+    hs, t_out, t_in = once()
+    ok = True
+    for i in range(0, victims, 9):  # bit-exact spot check of every 9th victim, all layers
+        a = bk._pool[:, :, src[i]]
+        b = bk._pool[:, :, dst[i]]
+        ok = ok and bool(torch.equal(a, b))
+    for h in hs:
+        sw.release(h)
+    return {"victims": victims, "tokens": toks, "bytes_per_direction": int(per_dir),
+            "d2h_gbs": round(per_dir / t_out / 1e9, 2), "h2d_gbs": round(per_dir / t_in / 1e9, 2),
+            "bit_exact_spot_check": ok, "timing": "host wall clock around issue + wait"}
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--seed", type=int, default=2026)
+    ap.add_argument("--pool-frac", type=float, default=0.9)
+    ap.add_argument("--max-graphs", type=int, default=32)
+    ap.add_argument("--e2e-steps", type=int, default=50)
+    ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU oracle timing (0 = skip)")
+    ap.add_argument("--no-swap", dest="swap", action="store_false")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    if args.impl == "reference":
+        args.steps_ref = max(1, min(args.steps, 100))
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,200 @@
+/*
+ * pkv.h — C ABI of the B200 paged-KV hot path (libpkv.so).
+ *
+ * Plain pointers, sizes and a CUDA stream handle; no torch or C++ types.
+ * Every function returns an int status (PKV_OK on success) and never aborts;
+ * pkv_last_error() returns a message for the calling thread's last failure.
+ * Arguments are validated on the host before anything touches the device.
+ *
+ * Device pointers are raw CUDA device addresses; `stream` is a cudaStream_t
+ * (NULL = legacy default stream).
+ *
+ * Pool layout (one allocation per pool, per device):
+ *     [num_layers][2 (K,V)][num_blocks][block_size][n_kv_heads][head_dim]
+ * so layer l's K (resp. V) is the contiguous slab
+ *     base + (2*l + 0|1) * num_blocks * block_size * row_bytes,
+ * row_bytes = n_kv_heads * head_dim * elem_size — exactly the per-layer
+ * [num_blocks, block_size, n_kv_heads, head_dim] tensors the reference's
+ * backends expose as k_pool[l] / v_pool[l] (serving/backends/paged_torch.py:124-137).
+ *
+ * Page-table inputs follow the reference's BatchMeta contract
+ * (docs/ARCHITECTURE.md:88-120): int32 CSR triple kv_indptr / kv_indices /
+ * kv_last_page_len, int32 cu_query_lens and slot_mapping.
+ */
+#ifndef PKV_H_
+#define PKV_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define PKV_API __attribute__((visibility("default")))
+#else
+#define PKV_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes -------------------------------------------------------- */
+#define PKV_OK 0
+#define PKV_ERR_ARG 1          /* invalid argument, detected on the host        */
+#define PKV_ERR_UNSUPPORTED 2  /* geometry / dtype no kernel here handles      */
+#define PKV_ERR_CUDA 3         /* a CUDA runtime call or launch failed          */
+#define PKV_ERR_DEVICE 4       /* a kernel recorded a violation (see flags)     */
+
+/* ---- device status flags (bits of the int32 a kernel may OR into) -------- */
+#define PKV_DEV_SLOT_OOB 0x1        /* slot / block id outside the pool          */
+#define PKV_DEV_META_BAD 0x2        /* CSR inconsistent (pages vs kv_len, lpl)   */
+#define PKV_DEV_QLEN_BAD 0x4        /* decode kernel saw a query length != 1     */
+#define PKV_DEV_WAIT_TIMEOUT 0x8    /* a bounded barrier wait gave up            */
+#define PKV_DEV_WORKSPACE 0x10      /* workspace smaller than the launch needs   */
+
+/* ---- element types ------------------------------------------------------- */
+#define PKV_F16 0
+#define PKV_BF16 1
+#define PKV_F32 2
+#define PKV_F64 3
+
+/* Pool descriptor. All fields are plain values; `base` is a device pointer. */
+typedef struct pkv_pool {
+  void* base;
+  int64_t num_blocks;
+  int32_t num_layers;
+  int32_t block_size;
+  int32_t n_kv_heads;
+  int32_t head_dim;
+  int32_t dtype; /* PKV_F16 / PKV_BF16 / PKV_F32 / PKV_F64 */
+  int32_t reserved;
+} pkv_pool;
+
+/* One step's page table on the device (BatchMeta's fields, int32). */
+typedef struct pkv_batch {
+  int32_t n_seqs;
+  int32_t n_tokens;          /* sum of query lengths (rows of q / out)       */
+  int64_t total_pages;       /* kv_indices length == kv_indptr[n_seqs]       */
+  const int32_t* cu_query_lens;   /* [n_seqs+1] */
+  const int32_t* kv_lens;         /* [n_seqs] (may be NULL: derived from CSR) */
+  const int32_t* kv_indptr;       /* [n_seqs+1] */
+  const int32_t* kv_indices;      /* [total_pages] */
+  const int32_t* kv_last_page_len;/* [n_seqs] */
+  int32_t* dev_status;            /* int32 device word kernels OR flags into; may be NULL */
+} pkv_batch;
+
+/* ---- library ------------------------------------------------------------- */
+
+/* Library version (major*10000 + minor*100 + patch). */
+PKV_API int pkv_version(void);
+
+/* Message of the calling thread's last non-OK status ("" if none). */
+PKV_API const char* pkv_last_error(void);
+
+/* ---- KV-append ----------------------------------------------------------
+ * Replaces PagedTorchBackend.append_kv (serving/backends/paged_torch.py:209-276)
+ * and FlashInferBackend.append_kv (serving/backends/flashinfer_backend.py:443-512):
+ * pool.view(-1, H, D)[slot_mapping[t]] = k[t] (and v), for layer `layer`.
+ * k, v: device [n_tokens][n_kv_heads][head_dim] contiguous, in the pool dtype.
+ * Idempotent. Slots outside [0, num_blocks*block_size) are skipped and flagged
+ * PKV_DEV_SLOT_OOB in *dev_status (if given). */
+PKV_API int pkv_append_kv(const pkv_pool* pool, int32_t layer, const void* k, const void* v,
+                  const int32_t* slot_mapping, int64_t n_tokens, int32_t* dev_status,
+                  void* stream);
+
+/* ---- attention ------------------------------------------------------------
+ * Replaces PagedTorchBackend.attend (serving/backends/paged_torch.py:280-485) and
+ * FlashInferBackend.attend / _ensure_planned (serving/backends/flashinfer_backend.py:516-676):
+ * out[t, h] = softmax(scale * q[t,h] . K[s, 0..limit]) V[s, ..] over the
+ * sequence's pages in listed order, query head h reading KV head
+ * h / (n_heads / n_kv_heads), bottom-right causal limit kv_len - q_len + j.
+ * q, out: device [n_tokens][n_heads][head_dim] in the pool dtype.
+ *
+ * `decode_hint` != 0 selects the split-K decode kernel, which requires every
+ * query length to be 1 (checked on the device: PKV_DEV_QLEN_BAD). Workspace
+ * (device, 256-byte aligned) of at least pkv_attend_workspace_size() bytes must
+ * be given; its counters must be zero before the first call on it and are left
+ * zero by every call. */
+PKV_API size_t pkv_attend_workspace_size(const pkv_pool* pool, int32_t n_heads, int32_t n_seqs,
+                                 int64_t total_pages, int32_t decode_hint);
+PKV_API int pkv_attend(const pkv_pool* pool, int32_t layer, int32_t n_heads, const void* q, void* out,
+               float scale, const pkv_batch* batch, int32_t decode_hint, void* workspace,
+               size_t workspace_bytes, void* stream);
+
+/* Build the per-step page schedule the decode kernel reads (once per step,
+ * reused by every layer's pkv_attend with the same batch and workspace). Also
+ * validates the CSR on the device (PKV_DEV_META_BAD / PKV_DEV_SLOT_OOB /
+ * PKV_DEV_QLEN_BAD). pkv_attend is pkv_plan (decode only) followed by
+ * pkv_attend_planned; a caller attending every layer of one step plans once. */
+PKV_API int pkv_plan(const pkv_pool* pool, int32_t n_heads, const pkv_batch* batch, void* workspace,
+             size_t workspace_bytes, void* stream);
+PKV_API int pkv_attend_planned(const pkv_pool* pool, int32_t layer, int32_t n_heads, const void* q,
+                       void* out, float scale, const pkv_batch* batch, int32_t decode_hint,
+                       void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- copy-on-write ---------------------------------------------------------
+ * Replaces PagedTorchBackend.copy_block (serving/backends/paged_torch.py:181-207)
+ * and FlashInferBackend.copy_block (flashinfer_backend.py:415-441), batched:
+ * for every pair i, block dst[i] := block src[i] in every layer, K and V, in one
+ * launch. src/dst: device int32 [n_pairs]. Pairs with src == dst are no-ops.
+ * The dst set must not intersect the src set (checked by the host wrapper);
+ * ids outside the pool are skipped and flagged PKV_DEV_SLOT_OOB. */
+PKV_API int pkv_copy_blocks(const pkv_pool* pool, const int32_t* src, const int32_t* dst,
+                    int64_t n_pairs, int32_t* dev_status, void* stream);
+
+/* The reference's exact signature, copy_block(src, dst), ids by value:
+ * PKV_ERR_ARG when either id is outside [0, num_blocks) (the reference raises
+ * IndexError, paged_torch.py:199-202); src == dst is a no-op. */
+PKV_API int pkv_copy_block(const pkv_pool* pool, int64_t src, int64_t dst, void* stream);
+
+/* ---- swap gather / scatter ------------------------------------------------
+ * Replace KVSwapSpace._to_host / _from_host (serving/scheduler/preemption.py:490-523).
+ * Host layout of a swapped sequence (the SwapHandle's k / v,
+ * preemption.py:303-333): [num_layers][nb][block_size][n_kv_heads][head_dim],
+ * K and V in separate buffers, block i of the handle = block_ids[i].
+ *
+ * pkv_swap_gather:  staging[(kv*L + l)*nb + i] = pool block block_ids[i], layer l
+ * pkv_swap_scatter: the reverse. `staging` is device memory holding the two
+ * host buffers back to back (K then V): 2 * L * nb * block_bytes. */
+PKV_API int pkv_swap_gather(const pkv_pool* pool, const int32_t* block_ids, int64_t nb, void* staging,
+                    int32_t* dev_status, void* stream);
+PKV_API int pkv_swap_scatter(const pkv_pool* pool, const int32_t* block_ids, int64_t nb,
+                     const void* staging, int32_t* dev_status, void* stream);
+
+/* Asynchronous swap engine: device gather into a bounded, double-buffered
+ * staging area, copy-engine transfers to/from pinned host memory on a private
+ * stream, events ordering it against the caller's compute stream. */
+typedef struct pkv_swapper pkv_swapper;
+
+/* `staging` (device) of `staging_bytes` is borrowed for the swapper's lifetime. */
+PKV_API int pkv_swapper_create(void* staging, size_t staging_bytes, pkv_swapper** out);
+PKV_API int pkv_swapper_destroy(pkv_swapper* sw);
+
+/* Swap-out of one sequence: reads blocks block_ids[0..nb) (device int32) of every
+ * layer into pinned host buffers host_k / host_v (each L*nb*block_bytes).
+ * Ordering: starts after all work already queued on `compute_stream`; work queued
+ * on `compute_stream` after this call starts only after the device has finished
+ * READING the blocks, so the caller may free the blocks as soon as this returns.
+ * The host buffers are complete once pkv_swapper_wait(sw, ticket) returns, where
+ * *ticket is set to this operation's ticket. */
+PKV_API int pkv_swap_out(pkv_swapper* sw, const pkv_pool* pool, const int32_t* block_ids, int64_t nb,
+                 void* host_k, void* host_v, void* compute_stream, int32_t* dev_status,
+                 uint64_t* ticket);
+
+/* Swap-in: writes host_k / host_v into blocks block_ids[0..nb) of every layer.
+ * Starts after work already queued on `compute_stream`; work queued on
+ * `compute_stream` afterwards sees the restored blocks. The host buffers may be
+ * released once pkv_swapper_wait(sw, ticket) returns. */
+PKV_API int pkv_swap_in(pkv_swapper* sw, const pkv_pool* pool, const int32_t* block_ids, int64_t nb,
+                const void* host_k, const void* host_v, void* compute_stream,
+                int32_t* dev_status, uint64_t* ticket);
+
+/* Block the host until operation `ticket` (0 = everything issued) completed. */
+PKV_API int pkv_swapper_wait(pkv_swapper* sw, uint64_t ticket);
+/* 1 if `ticket` completed, 0 if still in flight. */
+PKV_API int pkv_swapper_done(pkv_swapper* sw, uint64_t ticket);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PKV_H_ */

@@ -1,0 +1,31 @@
+"""
+llm_serving_layer_b200 — B200-native (sm_100a) paged-KV hot path for the
+``llm_serving_layer`` serving system.
+
+Drop-ins behind the reference's own interfaces:
+
+* ``B200PagedBackend`` — attention backend (``append_kv`` / ``attend`` /
+  ``copy_block``), replacing ``serving.backends.paged_torch.PagedTorchBackend``
+  and ``serving.backends.flashinfer_backend.FlashInferBackend``;
+* ``B200SwapSpace`` — preemption swap engine, replacing
+  ``serving.scheduler.preemption.KVSwapSpace``;
+* ``BatchMeta`` / ``build_meta`` — the engine's step descriptor (field-for-field)
+  and a vectorised assembler.
+
+All compute runs in ``_lib/libpkv.so`` (hand-written CUDA, C ABI in
+``include/pkv.h``); build it with ``python -m llm_serving_layer_b200.build``.
+"""
+
+from .backend import B200PagedBackend
+from .meta import AttentionBackend, BatchMeta, build_meta
+from .swap import B200SwapSpace, SwapHandle, SwapSpaceFull
+
+__all__ = [
+    "B200PagedBackend",
+    "B200SwapSpace",
+    "SwapHandle",
+    "SwapSpaceFull",
+    "BatchMeta",
+    "AttentionBackend",
+    "build_meta",
+]

@@ -108,18 +108,19 @@ def attend_reference(
 ) -> np.ndarray:
     """The reference's attention, step for step (``paged_torch.py:280-346,400-485``).
 
-    Per sequence: gather its pages, expand KV heads with interleave (query head
-    ``h`` reads KV head ``h // groups``), scores ``q·kᵀ`` in float32 times
-    ``scale``, bottom-right causal mask ``triu(kv_len - q_len + 1)`` when
-    ``q_len > 1``, float32 softmax, probabilities cast to the pool dtype, then
-    ``probs @ v`` in the pool dtype. Returns ``(tokens, n_heads, head_dim)`` in
-    the pool dtype.
+    Per sequence: gather its pages, query head ``h`` reads KV head
+    ``h // groups`` (the ``repeat_interleave`` mapping, done here by grouping
+    the query heads of one KV head instead of copying K/V), scores ``q·kᵀ`` in
+    float32 times ``scale``, bottom-right causal mask ``triu(kv_len - q_len + 1)``
+    when ``q_len > 1``, float32 softmax, probabilities cast to the pool dtype,
+    then ``probs @ v`` in the pool dtype. Returns ``(tokens, n_heads, head_dim)``
+    in the pool dtype.
     """
     m = meta_arrays(meta)
     dt = k_pool_l.dtype
     T, Hq, D = q.shape
     Hkv = k_pool_l.shape[2]
-    groups = Hq // Hkv
+    g = Hq // Hkv
     out = np.zeros((T, Hq, D), dtype=dt)
     cu, ql, kl = m["cu_query_lens"], m["query_lens"], m["kv_lens"]
     ip, idx, lp = m["kv_indptr"], m["kv_indices"], m["kv_last_page_len"]
@@ -128,20 +129,19 @@ def attend_reference(
         if q_len == 0:
             continue
         pages = idx[ip[i]: ip[i + 1]]
-        k = _gather(k_pool_l, pages, kv_len, int(lp[i]))
+        k = _gather(k_pool_l, pages, kv_len, int(lp[i]))  # (kv, Hkv, D)
         v = _gather(v_pool_l, pages, kv_len, int(lp[i]))
-        k = np.repeat(k, groups, axis=1).transpose(1, 0, 2)  # (Hq, kv, D)
-        v = np.repeat(v, groups, axis=1).transpose(1, 0, 2)
-        qh = q[cu[i]: cu[i + 1]].transpose(1, 0, 2)  # (Hq, q_len, D)
-        scores = np.matmul(qh.astype(np.float32), k.astype(np.float32).transpose(0, 2, 1))
-        scores = (scores * np.float32(scale)).astype(np.float32)
+        # (q_len, Hq, D) -> (Hkv, g*q_len, D): row (j, t) of KV head c is query head c*g + j
+        qg = q[cu[i]: cu[i + 1]].reshape(q_len, Hkv, g, D).transpose(1, 2, 0, 3).reshape(Hkv, g * q_len, D)
+        scores = np.matmul(qg.astype(np.float32), k.astype(np.float32).transpose(1, 2, 0))
+        scores = (scores * np.float32(scale)).reshape(Hkv, g, q_len, kv_len)
         if q_len > 1:
             off = kv_len - q_len
             mask = np.triu(np.full((q_len, kv_len), -np.inf, dtype=np.float32), k=off + 1)
-            scores = scores + mask[None]
-        probs = _softmax_f32(scores).astype(dt)
-        o = np.matmul(probs, v).astype(dt)  # (Hq, q_len, D) in the pool dtype
-        out[cu[i]: cu[i + 1]] = o.transpose(1, 0, 2)
+            scores = scores + mask
+        probs = _softmax_f32(scores).astype(dt).reshape(Hkv, g * q_len, kv_len)
+        o = np.matmul(probs, v.transpose(1, 0, 2)).astype(dt)  # pool dtype
+        out[cu[i]: cu[i + 1]] = o.reshape(Hkv, g, q_len, D).transpose(2, 0, 1, 3).reshape(q_len, Hq, D)
     return out
 
 
