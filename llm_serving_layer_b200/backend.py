@@ -260,6 +260,11 @@ class B200PagedBackend:
         else:
             mql = getattr(meta, "max_query_len", None)
             decode = (int(mql) == 1) if mql is not None else not bool(meta.is_prefill)
+        if decode and n_tokens != n:
+            raise ValueError(
+                f"BatchMeta describes a decode step (is_prefill=False) but has {n_tokens} tokens for "
+                f"{n} sequences; a decode step has exactly one query per sequence"
+            )
         t = {
             "cu": self._i32(meta.cu_query_lens),
             "kl": self._i32(meta.kv_lens) if getattr(meta, "kv_lens", None) is not None else None,

@@ -352,10 +352,8 @@ __global__ void __launch_bounds__(256) decode_kernel(const __grid_constant__ CUt
         }
       }
       __syncwarp();
-      if (lane < GROUPS * 8) {
-        uint4* dst = reinterpret_cast<uint4*>(out + (int64_t(seq) * a.n_heads + h * GROUPS) * DK_D);
-        dst[lane] = reinterpret_cast<const uint4*>(ostage)[lane];
-      }
+      uint4* dst = reinterpret_cast<uint4*>(out + (int64_t(seq) * a.n_heads + h * GROUPS) * DK_D);
+      for (int ch = lane; ch < GROUPS * 8; ch += 32) dst[ch] = reinterpret_cast<const uint4*>(ostage)[ch];
       __syncwarp();
     } else {
       // a piece of a sequence cut by a range boundary: write (m, l, O/l)
