@@ -18,6 +18,7 @@
 //                   mixed batches): one warp per (token, query head), CUDA cores.
 #include <algorithm>
 #include <array>
+#include <cstdlib>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -29,9 +30,10 @@ namespace {
 
 constexpr int DK_D = 64;       // head_dim of the decode kernel
 constexpr int DK_P = 16;       // tokens per page of the decode kernel
-constexpr int DK_TILE = DK_P * DK_D * 2;   // one [16 x 64] 16-bit tile: 2 KiB
-constexpr int DK_STAGE = 2 * DK_TILE;      // K tile + V tile
-constexpr int DK_NST = 3;                  // ring depth per warp
+constexpr int DK_NST = 6;                  // default ring depth (pages in flight per CTA)
+constexpr int DK_MERGE_CHUNK = 16;         // split-K pieces merged per pass
+constexpr int DK_MERGE_HEADS = 64;         // query heads of the decode kernel (n_heads <= 64)
+constexpr int DK_MERGE_PER = 8;            // merged outputs per consumer thread per pass
 
 // ---------------------------------------------------------------- workspace
 struct WsLayout {
@@ -136,22 +138,32 @@ __device__ __forceinline__ void load_q_frag(const T* __restrict__ q, int row, in
   }
 }
 
-template <typename T, int GROUPS, int NST>
-__global__ void __launch_bounds__(256) decode_kernel(const __grid_constant__ CUtensorMap tmap,
-                                                     const DecodeArgs a) {
+// One CTA = one producer warp + one consumer warp per KV head. The producer
+// streams whole pages: one TMA box per page for K and one for V, each the full
+// contiguous 16 KiB [16 tok][8 heads][64] page, read through a permuted view of
+// the pool (dims D, T, H) so that it lands in shared memory as [head][tok][64]
+// with the 128B swizzle keyed on the token (conflict-free ldmatrix for a head's
+// 16 tokens). Consumer warp h reads its head's 2 KiB slice of each stage.
+template <typename T, int GROUPS, int NST, int MINB>
+__global__ void __launch_bounds__(288, MINB) decode_kernel(const __grid_constant__ CUtensorMap tmap,
+                                                           const DecodeArgs a) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
-  // 1024-byte alignment for the 128B-swizzle pattern of the TMA tiles
   unsigned char* smem = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const int n_warps = blockDim.x >> 5;
+  const int n_cons = (blockDim.x >> 5) - 1;  // consumer warps == KV heads
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, c4 = lane & 3;
-  unsigned char* ring = smem + size_t(warp) * NST * DK_STAGE;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + size_t(n_warps) * NST * DK_STAGE) + warp * NST;
-  T* ostage = reinterpret_cast<T*>(smem + size_t(n_warps) * NST * DK_STAGE +
-                                   bar_bytes(n_warps, NST)) +
-              size_t(warp) * GROUPS * DK_D;
+  constexpr int PAGE = DK_P * DK_D * 8 * 2;  // 16 KiB: one page of one layer, K or V (8 heads)
+  constexpr int STAGE = 2 * PAGE;
+  unsigned char* stages = smem;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + size_t(NST) * STAGE);
+  uint64_t* empty = full + NST;
+  T* ostage_all = reinterpret_cast<T*>(smem + size_t(NST) * STAGE + bar_bytes(2, NST));
   __shared__ int s_last;
+  // merge scratch: per-head running max / normaliser / carry and per-piece weights
+  __shared__ float s_mrg_m[DK_MERGE_HEADS], s_mrg_W[DK_MERGE_HEADS], s_mrg_scale[DK_MERGE_HEADS];
+  __shared__ float s_mrg_w[DK_MERGE_CHUNK * DK_MERGE_HEADS];
+  __shared__ float s_mrg_acc[DK_MERGE_HEADS * DK_D];
 
   const int64_t P = a.total_pages;
   const int G = gridDim.x;
@@ -159,20 +171,20 @@ __global__ void __launch_bounds__(256) decode_kernel(const __grid_constant__ CUt
   const int64_t p0 = int64_t(c) * P / G, p1 = int64_t(c + 1) * P / G;
   if (p0 >= p1) return;
   const int R = int(p1 - p0);
-  const int h = warp;  // this warp's KV head
-  const T* q = static_cast<const T*>(a.q);
-  T* out = static_cast<T*>(a.out);
 
-  if (lane == 0) {
+  if (threadIdx.x == 0) {
     prefetch_tmap(&tmap);
-    for (int i = 0; i < NST; ++i) mbar_init(&bars[i], 1);
+    for (int i = 0; i < NST; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], n_cons);
+    }
     fence_mbar_init();
   }
-  __syncwarp();
+  __syncthreads();
 
   // page descriptors: lane j holds window entries [wb + j] (cur) and [wb + 32 + j] (nxt)
   int wb = 0;
-  int2 dcur = make_int2(0, 0), dnxt = make_int2(0, 0);
+  int2 dcur = make_int2(-1, -1), dnxt = make_int2(-1, -1);
   if (lane < R) dcur = a.desc[p0 + lane];
   if (32 + lane < R) dnxt = a.desc[p0 + 32 + lane];
   auto desc_at = [&](int i) -> int2 {  // uniform i in [wb, wb + 64)
@@ -182,59 +194,73 @@ __global__ void __launch_bounds__(256) decode_kernel(const __grid_constant__ CUt
     d.y = __shfl_sync(0xffffffffu, in_cur ? dcur.y : dnxt.y, i & 31);
     return d;
   };
-  const int kv_coord = 2 * a.layer;
-  auto issue = [&](int i, int2 d) {  // lane 0 only
-    unsigned char* dst = ring + (i % NST) * DK_STAGE;
-    uint64_t* bar = &bars[i % NST];
-    mbar_arrive_expect_tx(bar, DK_STAGE);
-    tma_load_4d(dst, &tmap, bar, 0, h, d.x * DK_P, kv_coord);
-    tma_load_4d(dst + DK_TILE, &tmap, bar, 0, h, d.x * DK_P, kv_coord + 1);
-  };
-  {
-    const int npro = R < NST ? R : NST;
-    for (int i = 0; i < npro; ++i) {
-      const int2 d = desc_at(i);
-      if (lane == 0) issue(i, d);
+  auto slide = [&](int i) {
+    if (i == wb + 32) {
+      wb += 32;
+      dcur = dnxt;
+      dnxt = make_int2(-1, -1);
+      if (wb + 32 + lane < R) dnxt = a.desc[p0 + wb + 32 + lane];
     }
+  };
+  const int kv_coord = 2 * a.layer;
+
+  if (warp == n_cons) {
+    // ---------------- producer warp
+    bool dead = false;
+    for (int i = 0; i < R; ++i) {
+      slide(i);
+      const int2 d = desc_at(i);
+      const int st = i % NST;
+      if (lane == 0 && !dead) {
+        if (i >= NST && !mbar_wait_bounded(&empty[st], ((i / NST) - 1) & 1, a.st)) dead = true;
+        if (!dead) {
+          unsigned char* dst = stages + size_t(st) * STAGE;
+          mbar_arrive_expect_tx(&full[st], 2u * n_cons * DK_P * DK_D * 2);
+          // a rejected page (id -1) reads the zero fill of a negative coordinate
+          tma_load_4d(dst, &tmap, &full[st], 0, d.x * DK_P, 0, kv_coord);
+          tma_load_4d(dst + PAGE, &tmap, &full[st], 0, d.x * DK_P, 0, kv_coord + 1);
+        }
+      }
+      __syncwarp();
+    }
+    return;
   }
 
-  // per-sequence running state (this thread: heads 2*c4, 2*c4+1 of the group)
+  // ---------------- consumer warp h
+  const int h = warp;
+  const T* q = static_cast<const T*>(a.q);
+  T* out = static_cast<T*>(a.out);
+  T* ostage = ostage_all + size_t(h) * GROUPS * DK_D;
+  const int n_cons_threads = n_cons * 32;
+  auto cons_sync = [&]() { asm volatile("bar.sync 1, %0;" ::"r"(n_cons_threads) : "memory"); };
+
   uint32_t qb[4][2], qn[4][2];
   float o[4][4];
   float m0 = -1e30f, m1 = -1e30f, l0 = 0.f, l1 = 0.f;
   int cur_seq = -1, nxt_seq = -1;
   bool seen_first = false, dead = false;
+  int64_t seq_fa = 0, seq_fb = 0;
   const int first_seq = desc_at(0).y >> 7;
 
-  // ldmatrix lane addressing inside a 128B-swizzled [16 x 64] tile
   const int k_tok = (lane & 7) + ((lane >> 3) & 1) * 8, k_chk = lane >> 4;
   const int v_tok = (lane & 7) + (lane >> 4) * 8, v_chk = (lane >> 3) & 1;
 
   for (int i = 0; i < R; ++i) {
-    if (i == wb + 32) {  // slide the descriptor window
-      wb += 32;
-      dcur = dnxt;
-      dnxt = make_int2(0, 0);
-      if (wb + 32 + lane < R) dnxt = a.desc[p0 + wb + 32 + lane];
-    }
+    slide(i);
     const int2 d = desc_at(i);
     const int seq = d.y >> 7;
     const bool is_first = (d.y >> 6) & 1, is_last = (d.y >> 5) & 1;
     const int valid = d.y & 31;
+    const int st = i % NST;
+    unsigned char* kt = stages + size_t(st) * STAGE + h * (DK_P * DK_D * 2);
+    unsigned char* vt = kt + PAGE;
+    if (!dead && !mbar_wait_bounded(&full[st], (i / NST) & 1, a.st)) dead = true;
+
     if (seq < 0 || seq >= a.n_seqs || valid < 1 || valid > DK_P) {
-      // a page of a sequence the plan rejected (descriptor left at -1): its
-      // stage still has to be drained and refilled, but nothing is computed
+      // a page of a sequence the plan rejected: release the stage, compute nothing
       if (lane == 0 && !dead) flag(a.st, PKV_DEV_META_BAD);
-      const int stg = i % NST;
-      if (!dead && !mbar_wait_bounded(&bars[stg], (i / NST) & 1, a.st)) dead = true;
       __syncwarp();
-      if (!dead && i + NST < R) {
-        const int2 dn = desc_at(i + NST);
-        if (lane == 0) {
-          fence_proxy_async_smem();
-          issue(i + NST, dn);
-        }
-      }
+      if (lane == 0) asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&empty[st])) : "memory");
       continue;
     }
     if (seq != cur_seq) {
@@ -246,6 +272,8 @@ __global__ void __launch_bounds__(256) decode_kernel(const __grid_constant__ CUt
       }
       cur_seq = seq;
       nxt_seq = seq + 1;
+      seq_fa = a.kv_indptr[seq];  // needed only if the sequence ends split
+      seq_fb = a.kv_indptr[seq + 1];
       if (nxt_seq < a.n_seqs) load_q_frag<T, GROUPS>(q, nxt_seq, a.n_heads, h, g, c4, qn);
 #pragma unroll
       for (int mt = 0; mt < 4; ++mt)
@@ -256,29 +284,25 @@ __global__ void __launch_bounds__(256) decode_kernel(const __grid_constant__ CUt
       seen_first = is_first;
     }
 
-    const int stg = i % NST;
-    unsigned char* kt = ring + stg * DK_STAGE;
-    unsigned char* vt = kt + DK_TILE;
-    // a wait that gives up marks the warp dead: it stops issuing copies and
-    // runs the rest of its loop on whatever is in shared memory (flagged)
-    if (!dead && !mbar_wait_bounded(&bars[stg], (i / NST) & 1, a.st)) dead = true;
-
-    if (valid < DK_P) {  // never let the unwritten tail of a last page reach P.V
+    const bool zeroed = valid < DK_P;
+    if (zeroed) {  // never let the unwritten tail of a last page reach P.V
       for (int r = valid * 8 + lane; r < DK_P * 8; r += 32)
         reinterpret_cast<uint4*>(vt)[r] = make_uint4(0u, 0u, 0u, 0u);
       __syncwarp();
     }
 
     // S^T[16 tok x 8 heads] = K[16 x 64] . Q^T[64 x 8]
-    float s[4] = {0.f, 0.f, 0.f, 0.f};
+    float s[4] = {0.f, 0.f, 0.f, 0.f}, s2[4] = {0.f, 0.f, 0.f, 0.f};
     const uint32_t kbase = smem_u32(kt);
 #pragma unroll
-    for (int ks = 0; ks < 4; ++ks) {
+    for (int ks = 0; ks < 4; ++ks) {  // two accumulators halve the dependent mma chain
       uint32_t af[4];
       const int chunk = 2 * ks + k_chk;
       ldsm_x4(af[0], af[1], af[2], af[3], kbase + k_tok * 128 + ((chunk ^ (k_tok & 7)) << 4));
-      MmaOp<T>::run(s, af, qb[ks][0], qb[ks][1]);
+      MmaOp<T>::run((ks & 1) ? s2 : s, af, qb[ks][0], qb[ks][1]);
     }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) s[e] += s2[e];
     // rows g and g+8 are tokens; columns 2*c4, 2*c4+1 are heads of the group
     const bool v0 = g < valid, v1 = (g + 8) < valid;
     s[0] = v0 ? s[0] * a.scale_log2 : -INFINITY;
@@ -318,12 +342,9 @@ __global__ void __launch_bounds__(256) decode_kernel(const __grid_constant__ CUt
       MmaOp<T>::run(o[mt], af, pb0, pb1);
     }
     __syncwarp();
-    if (!dead && i + NST < R) {  // refill this stage
-      const int2 dn = desc_at(i + NST);
-      if (lane == 0) {
-        fence_proxy_async_smem();
-        issue(i + NST, dn);
-      }
+    if (lane == 0) {  // release the stage to the producer
+      if (zeroed) fence_proxy_async_smem();  // the next TMA must land after the zero stores
+      asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&empty[st])) : "memory");
     }
 
     // end of this sequence within the CTA's range?
@@ -376,35 +397,84 @@ __global__ void __launch_bounds__(256) decode_kernel(const __grid_constant__ CUt
         if (j0 < GROUPS) { pb[j0 * (DK_D + 2) + DK_D] = m0; pb[j0 * (DK_D + 2) + DK_D + 1] = lt0; }
         if (j1 < GROUPS) { pb[j1 * (DK_D + 2) + DK_D] = m1; pb[j1 * (DK_D + 2) + DK_D + 1] = lt1; }
       }
-      __threadfence();
-      __syncthreads();
-      const int64_t fa = a.kv_indptr[seq], fb = a.kv_indptr[seq + 1];
+      cons_sync();  // every consumer warp's piece is written
+      const int64_t fa = seq_fa, fb = seq_fb;
       const int cf = cta_of(fa, P, G), cl = cta_of(fb - 1, P, G);
       if (threadIdx.x == 0) {
-        const int prev = atomicAdd(&a.counters[seq], 1);
+        // one acq_rel RMW at gpu scope: releases this CTA's piece (cumulative
+        // over the barrier above) and, for the last CTA, acquires the others'
+        int prev;
+        asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], 1;"
+                     : "=r"(prev) : "l"(a.counters + seq) : "memory");
         s_last = (prev == cl - cf);
       }
-      __syncthreads();
+      cons_sync();
       if (s_last) {
-        __threadfence();
+        // merge the pieces: per-head weights first (one pass over (m, l)),
+        // then every output element as one independent sweep over the pieces
         const int nh = a.n_heads;
-        for (int idx = threadIdx.x; idx < nh * DK_D; idx += blockDim.x) {
-          const int hh = idx / DK_D, dd = idx % DK_D;
-          float M = -1e30f;
-          for (int cc = cf; cc <= cl; ++cc) {
-            const int sl = (cc == cf && fa > int64_t(cc) * P / G) ? 1 : 0;
-            const float* pp = a.partial + (size_t(2 * cc + sl) * nh + hh) * (DK_D + 2);
-            M = fmaxf(M, __ldcg(pp + DK_D));
+        const int npieces = cl - cf + 1;
+        for (int p0m = 0; p0m < npieces; p0m += DK_MERGE_CHUNK) {
+          const int np = min(DK_MERGE_CHUNK, npieces - p0m);
+          for (int t = threadIdx.x; t < nh; t += n_cons_threads) {
+            float M = -1e30f;
+            for (int k = 0; k < np; ++k) {
+              const int cc = cf + p0m + k;
+              const int sl = (cc == cf && fa > int64_t(cc) * P / G) ? 1 : 0;
+              M = fmaxf(M, __ldcg(a.partial + (size_t(2 * cc + sl) * nh + t) * (DK_D + 2) + DK_D));
+            }
+            if (p0m > 0) M = fmaxf(M, s_mrg_m[t]);
+            float W = 0.f;
+            for (int k = 0; k < np; ++k) {
+              const int cc = cf + p0m + k;
+              const int sl = (cc == cf && fa > int64_t(cc) * P / G) ? 1 : 0;
+              const float* pp = a.partial + (size_t(2 * cc + sl) * nh + t) * (DK_D + 2);
+              const float w = __ldcg(pp + DK_D + 1) * ex2(__ldcg(pp + DK_D) - M);
+              s_mrg_w[k * DK_MERGE_HEADS + t] = w;
+              W += w;
+            }
+            // rescale what earlier chunks accumulated to this chunk's max
+            const float carry = (p0m > 0) ? ex2(s_mrg_m[t] - M) : 0.f;
+            s_mrg_scale[t] = carry;
+            s_mrg_W[t] = (p0m > 0 ? s_mrg_W[t] * carry : 0.f) + W;
+            s_mrg_m[t] = M;
           }
-          float wsum = 0.f, acc = 0.f;
-          for (int cc = cf; cc <= cl; ++cc) {
-            const int sl = (cc == cf && fa > int64_t(cc) * P / G) ? 1 : 0;
-            const float* pp = a.partial + (size_t(2 * cc + sl) * nh + hh) * (DK_D + 2);
-            const float w = __ldcg(pp + DK_D + 1) * ex2(__ldcg(pp + DK_D) - M);
-            wsum += w;
-            acc += w * __ldcg(pp + dd);
+          cons_sync();
+          // every thread owns DK_MERGE_PER outputs; all their loads are issued
+          // before any is consumed (one L2 round trip per pass, not one per output)
+          for (int base = 0; base < nh * DK_D; base += n_cons_threads * DK_MERGE_PER) {
+            float acc[DK_MERGE_PER];
+#pragma unroll
+            for (int r = 0; r < DK_MERGE_PER; ++r) {
+              const int idx = base + r * n_cons_threads + threadIdx.x;
+              acc[r] = (p0m > 0 && idx < nh * DK_D) ? s_mrg_acc[idx] * s_mrg_scale[idx / DK_D] : 0.f;
+            }
+            for (int k = 0; k < np; ++k) {
+              const int cc = cf + p0m + k;
+              const int sl = (cc == cf && fa > int64_t(cc) * P / G) ? 1 : 0;
+              const float* pp = a.partial + size_t(2 * cc + sl) * nh * (DK_D + 2);
+              float v[DK_MERGE_PER];
+#pragma unroll
+              for (int r = 0; r < DK_MERGE_PER; ++r) {
+                const int idx = base + r * n_cons_threads + threadIdx.x;
+                v[r] = idx < nh * DK_D ? __ldcg(pp + (idx / DK_D) * (DK_D + 2) + idx % DK_D) : 0.f;
+              }
+#pragma unroll
+              for (int r = 0; r < DK_MERGE_PER; ++r) {
+                const int idx = base + r * n_cons_threads + threadIdx.x;
+                if (idx < nh * DK_D) acc[r] += s_mrg_w[k * DK_MERGE_HEADS + idx / DK_D] * v[r];
+              }
+            }
+#pragma unroll
+            for (int r = 0; r < DK_MERGE_PER; ++r) {
+              const int idx = base + r * n_cons_threads + threadIdx.x;
+              if (idx >= nh * DK_D) continue;
+              const int hh = idx / DK_D, dd = idx % DK_D;
+              if (p0m + np < npieces) s_mrg_acc[idx] = acc[r];
+              else out[(int64_t(seq) * nh + hh) * DK_D + dd] = from_f<T>(acc[r] / s_mrg_W[hh]);
+            }
           }
-          out[(int64_t(seq) * nh + hh) * DK_D + dd] = from_f<T>(acc / wsum);
+          cons_sync();
         }
         if (threadIdx.x == 0) a.counters[seq] = 0;
       }
@@ -588,11 +658,15 @@ int get_tmap(const pkv_pool& p, CUtensorMap* out) {
   }
   const int es = elem_size(p.dtype);
   TmapEntry e{dev, p.base, p.num_blocks, p.num_layers, p.block_size, p.n_kv_heads, p.head_dim, p.dtype, {}};
-  const cuuint64_t dims[4] = {cuuint64_t(p.head_dim), cuuint64_t(p.n_kv_heads),
-                              cuuint64_t(p.num_blocks) * p.block_size, cuuint64_t(2) * p.num_layers};
-  const cuuint64_t strides[3] = {cuuint64_t(p.head_dim) * es, cuuint64_t(row_bytes(p)),
+  // Permuted view of the pool: dims (D, token slot, KV head, layer*2+kv) with
+  // strides (elem, row, head_dim*elem, slab). One box = one whole page of one
+  // layer's K or V, landing in shared memory as [head][token][D].
+  const cuuint64_t dims[4] = {cuuint64_t(p.head_dim), cuuint64_t(p.num_blocks) * p.block_size,
+                              cuuint64_t(p.n_kv_heads), cuuint64_t(2) * p.num_layers};
+  const cuuint64_t strides[3] = {cuuint64_t(row_bytes(p)), cuuint64_t(p.head_dim) * es,
                                  cuuint64_t(slab_bytes(p))};
-  const cuuint32_t box[4] = {cuuint32_t(p.head_dim), 1u, cuuint32_t(p.block_size), 1u};
+  const cuuint32_t box[4] = {cuuint32_t(p.head_dim), cuuint32_t(p.block_size),
+                             cuuint32_t(p.n_kv_heads), 1u};
   const cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
   const CUtensorMapDataType dt =
       p.dtype == PKV_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
@@ -615,14 +689,34 @@ bool decode_supported(const pkv_pool& p, int n_heads) {
   return gq == 1 || gq == 2 || gq == 4 || gq == 8;
 }
 
-size_t decode_smem(int n_kv_heads, int groups) {
-  return 1024 + size_t(n_kv_heads) * DK_NST * DK_STAGE + bar_bytes(n_kv_heads, DK_NST) +
-         size_t(n_kv_heads) * groups * DK_D * 2;
+size_t decode_smem(int n_kv_heads, int groups, int nst) {
+  const size_t stage = size_t(2) * DK_P * DK_D * 8 * 2;  // K + V page, 8 heads (boxes always 8 wide)
+  return 1024 + nst * stage + bar_bytes(2, nst) + size_t(n_kv_heads) * groups * DK_D * 2;
+}
+
+// Ring depth and CTAs per SM of the decode kernel. Defaults are the tuned
+// values; PKV_DECODE_NST (2, 3, 4 or 6) and PKV_DECODE_CTAS_PER_SM override them
+// for launch-shape sweeps.
+int decode_nst() {
+  static int v = [] {
+    const char* e = getenv("PKV_DECODE_NST");
+    const int n = e ? atoi(e) : DK_NST;
+    return (n == 2 || n == 3 || n == 4 || n == 6) ? n : DK_NST;
+  }();
+  return v;
+}
+int decode_ctas_per_sm_cap() {
+  static int v = [] {
+    const char* e = getenv("PKV_DECODE_CTAS_PER_SM");
+    const int n = e ? atoi(e) : 0;
+    return n > 0 ? n : 64;
+  }();
+  return v;
 }
 
 // CTAs of the decode kernel resident per SM, cached per (device, n_kv_heads);
 // also raises the kernel's dynamic shared-memory limit on first use per device.
-template <typename T, int GROUPS>
+template <typename T, int GROUPS, int NST, int MINB>
 int decode_grid_limit(int n_kv_heads) {
   static std::mutex mu;
   static std::vector<std::array<int, 9>> occ;
@@ -632,43 +726,55 @@ int decode_grid_limit(int n_kv_heads) {
   if ((int)occ.size() <= dev) occ.resize(dev + 1, std::array<int, 9>{});
   int& o = occ[dev][n_kv_heads];
   if (!o) {
-    auto fn = decode_kernel<T, GROUPS, DK_NST>;
-    const size_t sm = decode_smem(n_kv_heads, GROUPS);
+    auto fn = decode_kernel<T, GROUPS, NST, MINB>;
+    const size_t sm = decode_smem(n_kv_heads, GROUPS, NST);
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm));
     int v = 0;
-    if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, fn, 32 * n_kv_heads, sm);
+    if (e == cudaSuccess)
+      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, fn, 32 * (n_kv_heads + 1), sm);
     if (e != cudaSuccess) {
       cuda_fail(e, "decode kernel occupancy query");
       return -1;
     }
-    o = std::max(1, v);
+    o = std::max(1, std::min(v, decode_ctas_per_sm_cap()));
   }
   return o * num_sms();
 }
 
 int max_decode_grid() { return num_sms() * 8; }
 
-template <typename T, int GROUPS>
+template <typename T, int GROUPS, int NST, int MINB>
 int launch_decode_t(const pkv_pool& p, const CUtensorMap& tm, DecodeArgs& a, int64_t total_pages,
                     cudaStream_t s) {
-  int limit = decode_grid_limit<T, GROUPS>(p.n_kv_heads);
+  int limit = decode_grid_limit<T, GROUPS, NST, MINB>(p.n_kv_heads);
   if (limit <= 0) return PKV_ERR_CUDA;  // message already set
   limit = std::min(limit, max_decode_grid());
   const int grid = int(std::max<int64_t>(1, std::min<int64_t>(limit, total_pages)));
-  decode_kernel<T, GROUPS, DK_NST>
-      <<<grid, 32 * p.n_kv_heads, decode_smem(p.n_kv_heads, GROUPS), s>>>(tm, a);
+  decode_kernel<T, GROUPS, NST, MINB>
+      <<<grid, 32 * (p.n_kv_heads + 1), decode_smem(p.n_kv_heads, GROUPS, NST), s>>>(tm, a);
   PKV_CUDA_RET(cudaGetLastError());
   return PKV_OK;
+}
+
+template <typename T, int GROUPS>
+int launch_decode_n(const pkv_pool& p, const CUtensorMap& tm, DecodeArgs& a, int64_t tp,
+                    cudaStream_t s) {
+  switch (decode_nst()) {
+    case 2: return launch_decode_t<T, GROUPS, 2, 2>(p, tm, a, tp, s);
+    case 3: return launch_decode_t<T, GROUPS, 3, 2>(p, tm, a, tp, s);
+    case 4: return launch_decode_t<T, GROUPS, 4, 1>(p, tm, a, tp, s);
+    default: return launch_decode_t<T, GROUPS, 6, 1>(p, tm, a, tp, s);
+  }
 }
 
 template <typename T>
 int launch_decode_g(const pkv_pool& p, int groups, const CUtensorMap& tm, DecodeArgs& a,
                     int64_t tp, cudaStream_t s) {
   switch (groups) {
-    case 1: return launch_decode_t<T, 1>(p, tm, a, tp, s);
-    case 2: return launch_decode_t<T, 2>(p, tm, a, tp, s);
-    case 4: return launch_decode_t<T, 4>(p, tm, a, tp, s);
-    case 8: return launch_decode_t<T, 8>(p, tm, a, tp, s);
+    case 1: return launch_decode_n<T, 1>(p, tm, a, tp, s);
+    case 2: return launch_decode_n<T, 2>(p, tm, a, tp, s);
+    case 4: return launch_decode_n<T, 4>(p, tm, a, tp, s);
+    case 8: return launch_decode_n<T, 8>(p, tm, a, tp, s);
   }
   return fail(PKV_ERR_UNSUPPORTED, "decode kernel: unsupported GQA group size");
 }
