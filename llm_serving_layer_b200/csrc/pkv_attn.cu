@@ -30,16 +30,24 @@ namespace {
 
 constexpr int DK_D = 64;       // head_dim of the decode kernel
 constexpr int DK_P = 16;       // tokens per page of the decode kernel
-constexpr int DK_NST = 6;                  // default ring depth (pages in flight per CTA)
+constexpr int DK_NST = 4;                  // default ring depth (pages in flight per CTA)
 constexpr int DK_MERGE_CHUNK = 16;         // split-K pieces merged per pass
 constexpr int DK_MERGE_HEADS = 64;         // query heads of the decode kernel (n_heads <= 64)
-constexpr int DK_MERGE_PER = 8;            // merged outputs per consumer thread per pass
+constexpr int DK_U = 2;                    // pages folded per online-softmax update
+#ifndef DK_TAIL_FIRST
+#define DK_TAIL_FIRST 0                    // process the range's tail piece first
+#endif
+#ifndef DK_PRODUCER_SLEEP_NS
+#define DK_PRODUCER_SLEEP_NS 64            // producer back-off while the ring is full
+#endif
+constexpr int DK_MAXNREG = 168;            // 9 warps: 3 per SM sub-partition x 32 x 168 <= 16K registers
 
 // ---------------------------------------------------------------- workspace
 struct WsLayout {
-  size_t page_desc = 0;  // int2[total_pages]
+  size_t page_desc = 0;  // int4[total_pages]
   size_t counters = 0;   // int32[n_seqs]
-  size_t partial = 0;    // float[2 * grid][n_heads][D + 2]
+  size_t partial_o = 0;   // float[2 * grid][n_heads][D]
+  size_t partial_ml = 0;  // float2[2 * grid][n_heads]
   size_t total = 0;
 };
 
@@ -49,23 +57,26 @@ WsLayout ws_layout(int n_heads, int n_seqs, int64_t total_pages, int max_grid, i
   WsLayout w;
   size_t off = 0;
   w.page_desc = off;
-  off = align256(off + sizeof(int2) * size_t(std::max<int64_t>(total_pages, 1)));
+  off = align256(off + sizeof(int4) * size_t(std::max<int64_t>(total_pages, 1)));
   w.counters = off;
   off = align256(off + sizeof(int32_t) * size_t(std::max(n_seqs, 1)));
-  w.partial = off;
-  off = align256(off + sizeof(float) * size_t(2) * max_grid * n_heads * (head_dim + 2));
+  w.partial_o = off;
+  off = align256(off + sizeof(float) * size_t(2) * max_grid * n_heads * head_dim);
+  w.partial_ml = off;
+  off = align256(off + sizeof(float2) * size_t(2) * max_grid * n_heads);
   w.total = off;
   return w;
 }
 
 // ---------------------------------------------------------------- plan
-// page_desc[p] = {page id, (seq << 7) | (first << 6) | (last << 5) | valid}
+// page_desc[p] = {page id, (seq << 7) | (first << 6) | (last << 5) | valid,
+//                 first page of seq, one past its last page}
 __global__ void plan_kernel(const int32_t* __restrict__ kv_indptr,
                             const int32_t* __restrict__ kv_indices,
                             const int32_t* __restrict__ last_page_len,
                             const int32_t* __restrict__ kv_lens,
                             const int32_t* __restrict__ cu_q, int n_seqs, int64_t total_pages,
-                            int block_size, int64_t num_blocks, int2* __restrict__ desc,
+                            int block_size, int64_t num_blocks, int4* __restrict__ desc,
                             int32_t* __restrict__ counters, int check_decode, int32_t* st) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
@@ -93,7 +104,7 @@ __global__ void plan_kernel(const int32_t* __restrict__ kv_indptr,
     if (id < 0 || id >= num_blocks) flag(st, PKV_DEV_SLOT_OOB);
     const int first = (p == a), last = (p == b - 1);
     const int valid = last ? lpl : block_size;
-    desc[p] = make_int2(id, (s << 7) | (first << 6) | (last << 5) | valid);
+    desc[p] = make_int4(id, (s << 7) | (first << 6) | (last << 5) | valid, int(a), int(b));
   }
 }
 
@@ -102,8 +113,9 @@ struct DecodeArgs {
   const void* q;
   void* out;
   const int32_t* kv_indptr;
-  const int2* desc;
-  float* partial;
+  const int4* desc;
+  float* partial_o;    // [2 * grid][n_heads][D]   O / l of each split piece
+  float2* partial_ml;  // [2 * grid][n_heads]      (m, l) of each split piece
   int32_t* counters;
   int32_t* st;
   int64_t total_pages;
@@ -138,15 +150,174 @@ __device__ __forceinline__ void load_q_frag(const T* __restrict__ q, int row, in
   }
 }
 
-// One CTA = one producer warp + one consumer warp per KV head. The producer
+// Merge the split-K pieces cf..cl of sequence `seq` with `nthr` threads (tid
+// in [0, nthr)): per head, the running max M and normaliser W over the
+// pieces' (m, l), then every output element as sum_k w_k O_k / W. Pieces are
+// taken DK_MERGE_CHUNK at a time with a carry factor, so any number merges.
+// The participating threads synchronise with named barrier `bar` (nthr > 32)
+// or __syncwarp (one warp).
+template <typename T>
+__device__ __noinline__ void merge_pieces(const DecodeArgs& a, int seq, int64_t fa, int cf, int cl,
+                                          int64_t P, int G, int tid, int nthr, int bar,
+                                          float2* s_ml, float* sW, float* sM, float* sC,
+                                          float* s_acc) {
+  auto sync = [&]() {
+    if (nthr > 32) asm volatile("bar.sync %0, %1;" ::"r"(bar), "r"(nthr) : "memory");
+    else __syncwarp();
+  };
+  const int nh = a.n_heads;
+  const int npieces = cl - cf + 1;
+  T* out = static_cast<T*>(a.out) + int64_t(seq) * nh * DK_D;
+  auto slot_of = [&](int cc) { return 2 * cc + ((cc == cf && fa > int64_t(cc) * P / G) ? 1 : 0); };
+  for (int k0 = 0; k0 < npieces; k0 += DK_MERGE_CHUNK) {
+    const int np = min(DK_MERGE_CHUNK, npieces - k0);
+    for (int t = tid; t < np * nh; t += nthr) {
+      const int k = t / nh, hh = t % nh;
+      s_ml[k * DK_MERGE_HEADS + hh] = __ldcg(a.partial_ml + size_t(slot_of(cf + k0 + k)) * nh + hh);
+    }
+    sync();
+    for (int hh = tid; hh < nh; hh += nthr) {
+      float M = k0 ? sM[hh] : -1e30f;
+      for (int k = 0; k < np; ++k) M = fmaxf(M, s_ml[k * DK_MERGE_HEADS + hh].x);
+      float W = 0.f;
+      for (int k = 0; k < np; ++k) {
+        float2& ml = s_ml[k * DK_MERGE_HEADS + hh];
+        const float w = ml.y * ex2(ml.x - M);
+        ml.x = w;  // from here on .x is the piece's weight
+        W += w;
+      }
+      const float carry = k0 ? ex2(sM[hh] - M) : 0.f;
+      sC[hh] = carry;
+      sW[hh] = (k0 ? sW[hh] * carry : 0.f) + W;
+      sM[hh] = M;
+    }
+    sync();
+    const bool last = k0 + np == npieces;
+    const int per = nh * DK_D / nthr;  // outputs per thread (nthr divides nh * 64)
+    for (int r0 = 0; r0 < per; r0 += 8) {
+      float acc[8];
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        const int idx = (r0 + r) * nthr + tid;
+        acc[r] = (k0 && r0 + r < per) ? s_acc[idx] * sC[idx / DK_D] : 0.f;
+      }
+      for (int k = 0; k < np; ++k) {
+        const float* po = a.partial_o + size_t(slot_of(cf + k0 + k)) * nh * DK_D;
+        float v[8];
+#pragma unroll
+        for (int r = 0; r < 8; ++r) v[r] = (r0 + r < per) ? __ldcg(po + (r0 + r) * nthr + tid) : 0.f;
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+          const int idx = (r0 + r) * nthr + tid;
+          if (r0 + r < per) acc[r] += s_ml[k * DK_MERGE_HEADS + idx / DK_D].x * v[r];
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        const int idx = (r0 + r) * nthr + tid;
+        if (r0 + r >= per) continue;
+        if (last) out[idx] = from_f<T>(acc[r] / sW[idx / DK_D]);
+        else s_acc[idx] = acc[r];
+      }
+    }
+    sync();
+  }
+}
+
+// Attention of one warp's KV head over U consecutive pages of one sequence,
+// folded into the running (m, l, O) state with one online-softmax update.
+// kb[u] / vb[u]: shared addresses of page u's [16 tok x 64] K / V tiles (128B
+// swizzled); only the last page may be partial (valid_last tokens).
+template <typename T, int U>
+__device__ __forceinline__ void attend_pages(const uint32_t (&kb)[U], const uint32_t (&vb)[U],
+                                             int valid_last, const uint32_t (&qb)[4][2],
+                                             float (&o)[4][4], float& m0, float& m1, float& l0,
+                                             float& l1, float scale_log2, int k_tok, int k_chk,
+                                             int v_tok, int v_chk, int g) {
+  // S^T[16 tok x 8 heads] = K[16 x 64] . Q^T[64 x 8], per page
+  float s[U][4];
+#pragma unroll
+  for (int u = 0; u < U; ++u)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) s[u][e] = 0.f;
+#pragma unroll
+  for (int ks = 0; ks < 4; ++ks) {
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      uint32_t af[4];
+      const int chunk = 2 * ks + k_chk;
+      ldsm_x4(af[0], af[1], af[2], af[3], kb[u] + k_tok * 128 + ((chunk ^ (k_tok & 7)) << 4));
+      MmaOp<T>::run(s[u], af, qb[ks][0], qb[ks][1]);
+    }
+  }
+  // rows g and g+8 are tokens, columns 2*c4 and 2*c4+1 heads of the group
+  const bool v0 = g < valid_last, v1 = (g + 8) < valid_last;
+  float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    const bool a0 = (u < U - 1) || v0, a1 = (u < U - 1) || v1;
+    s[u][0] = a0 ? s[u][0] * scale_log2 : -INFINITY;
+    s[u][1] = a0 ? s[u][1] * scale_log2 : -INFINITY;
+    s[u][2] = a1 ? s[u][2] * scale_log2 : -INFINITY;
+    s[u][3] = a1 ? s[u][3] * scale_log2 : -INFINITY;
+    mx0 = fmaxf(mx0, fmaxf(s[u][0], s[u][2]));
+    mx1 = fmaxf(mx1, fmaxf(s[u][1], s[u][3]));
+  }
+#pragma unroll
+  for (int off = 4; off < 32; off <<= 1) {
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+  }
+  const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+  const float al0 = ex2(m0 - mn0), al1 = ex2(m1 - mn1);
+  m0 = mn0;
+  m1 = mn1;
+  float ls0 = 0.f, ls1 = 0.f;
+  uint32_t pb[U][2];
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    const float p00 = ex2(s[u][0] - mn0), p01 = ex2(s[u][1] - mn1);
+    const float p10 = ex2(s[u][2] - mn0), p11 = ex2(s[u][3] - mn1);
+    ls0 += p00 + p10;
+    ls1 += p01 + p11;
+    pb[u][0] = movmatrix_t(MmaOp<T>::pack(p00, p01));
+    pb[u][1] = movmatrix_t(MmaOp<T>::pack(p10, p11));
+  }
+  l0 = l0 * al0 + ls0;
+  l1 = l1 * al1 + ls1;
+#pragma unroll
+  for (int mt = 0; mt < 4; ++mt) {
+    o[mt][0] *= al0;
+    o[mt][2] *= al0;
+    o[mt][1] *= al1;
+    o[mt][3] *= al1;
+  }
+  // O^T[64 dims x 8 heads] += V^T[64 x 16] . P^T[16 x 8], per page
+#pragma unroll
+  for (int mt = 0; mt < 4; ++mt) {
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      uint32_t af[4];
+      const int chunk = 2 * mt + v_chk;
+      ldsm_x4_t(af[0], af[1], af[2], af[3], vb[u] + v_tok * 128 + ((chunk ^ (v_tok & 7)) << 4));
+      MmaOp<T>::run(o[mt], af, pb[u][0], pb[u][1]);
+    }
+  }
+}
+
+// One CTA = one consumer warp per KV head + one producer warp. The producer
 // streams whole pages: one TMA box per page for K and one for V, each the full
 // contiguous 16 KiB [16 tok][8 heads][64] page, read through a permuted view of
 // the pool (dims D, T, H) so that it lands in shared memory as [head][tok][64]
-// with the 128B swizzle keyed on the token (conflict-free ldmatrix for a head's
-// 16 tokens). Consumer warp h reads its head's 2 KiB slice of each stage.
+// with the 128B swizzle keyed on the token (conflict-free ldmatrix over a
+// head's 16 tokens). Consumer warp h reads its head's 2 KiB slice of each stage
+// and walks the range sequence piece by sequence piece, DK_U pages per
+// online-softmax update. A piece cut by a range boundary is written as a
+// partial (O/l, m, l) and counted in with one atomic; the CTA that completes
+// the sequence merges its pieces.
 template <typename T, int GROUPS, int NST, int MINB>
-__global__ void __launch_bounds__(288, MINB) decode_kernel(const __grid_constant__ CUtensorMap tmap,
-                                                           const DecodeArgs a) {
+__global__ void __maxnreg__(DK_MAXNREG) decode_kernel(const __grid_constant__ CUtensorMap tmap,
+                                                      const DecodeArgs a) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -158,12 +329,12 @@ __global__ void __launch_bounds__(288, MINB) decode_kernel(const __grid_constant
   unsigned char* stages = smem;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + size_t(NST) * STAGE);
   uint64_t* empty = full + NST;
-  T* ostage_all = reinterpret_cast<T*>(smem + size_t(NST) * STAGE + bar_bytes(2, NST));
-  __shared__ int s_last;
-  // merge scratch: per-head running max / normaliser / carry and per-piece weights
-  __shared__ float s_mrg_m[DK_MERGE_HEADS], s_mrg_W[DK_MERGE_HEADS], s_mrg_scale[DK_MERGE_HEADS];
-  __shared__ float s_mrg_w[DK_MERGE_CHUNK * DK_MERGE_HEADS];
+  float* ostage_all = reinterpret_cast<float*>(smem + size_t(NST) * STAGE + bar_bytes(2, NST));
+  // merge-warp scratch: (m, l) of a chunk of pieces per head, then their weights
+  __shared__ float2 s_ml[DK_MERGE_CHUNK * DK_MERGE_HEADS];
+  __shared__ float s_mrg_W[DK_MERGE_HEADS], s_mrg_M[DK_MERGE_HEADS], s_mrg_carry[DK_MERGE_HEADS];
   __shared__ float s_mrg_acc[DK_MERGE_HEADS * DK_D];
+  __shared__ int s_last;
 
   const int64_t P = a.total_pages;
   const int G = gridDim.x;
@@ -171,7 +342,6 @@ __global__ void __launch_bounds__(288, MINB) decode_kernel(const __grid_constant
   const int64_t p0 = int64_t(c) * P / G, p1 = int64_t(c + 1) * P / G;
   if (p0 >= p1) return;
   const int R = int(p1 - p0);
-
   if (threadIdx.x == 0) {
     prefetch_tmap(&tmap);
     for (int i = 0; i < NST; ++i) {
@@ -182,24 +352,53 @@ __global__ void __launch_bounds__(288, MINB) decode_kernel(const __grid_constant
   }
   __syncthreads();
 
+  // Processing order. The range's last sequence (tail piece T) and first
+  // sequence (head piece H) may be cut by the range's ends; T is taken first,
+  // then H, then the middle M, so that split pieces are published early and
+  // their merges overlap the consumers' remaining work.
+  const int4 dfirst = a.desc[p0], dlast = a.desc[p1 - 1];
+  int lenT = 0, lenH = 0;
+  int64_t hend = p0, tstart = p1;
+  {
+    const int sf = dfirst.y >> 7, sl = dlast.y >> 7;
+    if (DK_TAIL_FIRST && sf >= 0 && sl >= 0 && sf != sl && dfirst.w > p0 && dfirst.w <= p1 &&
+        dlast.z >= p0 && dlast.z < p1) {
+      hend = dfirst.w;
+      tstart = dlast.z;
+      lenT = int(p1 - tstart);
+      lenH = int(hend - p0);
+    }
+  }
+  auto pos = [&](int i) -> int64_t {  // processing step -> page index
+    if (i < lenT) return tstart + i;
+    if (i < lenT + lenH) return p0 + (i - lenT);
+    return (lenT ? hend : p0) + (i - lenT - lenH);
+  };
+  auto seg_end = [&](int i) -> int64_t {  // one past the last page of step i's segment
+    if (i < lenT) return p1;
+    if (i < lenT + lenH) return hend;
+    return lenT ? tstart : p1;
+  };
   // page descriptors: lane j holds window entries [wb + j] (cur) and [wb + 32 + j] (nxt)
   int wb = 0;
-  int2 dcur = make_int2(-1, -1), dnxt = make_int2(-1, -1);
-  if (lane < R) dcur = a.desc[p0 + lane];
-  if (32 + lane < R) dnxt = a.desc[p0 + 32 + lane];
-  auto desc_at = [&](int i) -> int2 {  // uniform i in [wb, wb + 64)
+  int4 dcur = make_int4(-1, -1, -1, -1), dnxt = make_int4(-1, -1, -1, -1);
+  if (lane < R) dcur = a.desc[pos(lane)];
+  if (32 + lane < R) dnxt = a.desc[pos(32 + lane)];
+  auto desc_at = [&](int i) -> int4 {  // uniform i in [wb, wb + 64)
     const bool in_cur = i < wb + 32;
-    int2 d;
+    int4 d;
     d.x = __shfl_sync(0xffffffffu, in_cur ? dcur.x : dnxt.x, i & 31);
     d.y = __shfl_sync(0xffffffffu, in_cur ? dcur.y : dnxt.y, i & 31);
+    d.z = __shfl_sync(0xffffffffu, in_cur ? dcur.z : dnxt.z, i & 31);
+    d.w = __shfl_sync(0xffffffffu, in_cur ? dcur.w : dnxt.w, i & 31);
     return d;
   };
-  auto slide = [&](int i) {
-    if (i == wb + 32) {
+  auto slide_to = [&](int i) {  // make [i, i + 32) resident (i advances by <= 32)
+    while (i >= wb + 32) {
       wb += 32;
       dcur = dnxt;
-      dnxt = make_int2(-1, -1);
-      if (wb + 32 + lane < R) dnxt = a.desc[p0 + wb + 32 + lane];
+      dnxt = make_int4(-1, -1, -1, -1);
+      if (wb + 32 + lane < R) dnxt = a.desc[pos(wb + 32 + lane)];
     }
   };
   const int kv_coord = 2 * a.layer;
@@ -208,11 +407,12 @@ __global__ void __launch_bounds__(288, MINB) decode_kernel(const __grid_constant
     // ---------------- producer warp
     bool dead = false;
     for (int i = 0; i < R; ++i) {
-      slide(i);
-      const int2 d = desc_at(i);
+      slide_to(i);
+      const int4 d = desc_at(i);
       const int st = i % NST;
       if (lane == 0 && !dead) {
-        if (i >= NST && !mbar_wait_bounded(&empty[st], ((i / NST) - 1) & 1, a.st)) dead = true;
+        if (i >= NST && !mbar_wait_bounded_sleepy(&empty[st], ((i / NST) - 1) & 1, a.st, DK_PRODUCER_SLEEP_NS))
+          dead = true;
         if (!dead) {
           unsigned char* dst = stages + size_t(st) * STAGE;
           mbar_arrive_expect_tx(&full[st], 2u * n_cons * DK_P * DK_D * 2);
@@ -230,126 +430,98 @@ __global__ void __launch_bounds__(288, MINB) decode_kernel(const __grid_constant
   const int h = warp;
   const T* q = static_cast<const T*>(a.q);
   T* out = static_cast<T*>(a.out);
-  T* ostage = ostage_all + size_t(h) * GROUPS * DK_D;
-  const int n_cons_threads = n_cons * 32;
-  auto cons_sync = [&]() { asm volatile("bar.sync 1, %0;" ::"r"(n_cons_threads) : "memory"); };
+  float* ostage = ostage_all + size_t(h) * GROUPS * DK_D;
+  bool dead = false;
+  auto wait_full = [&](int i) {
+    if (!dead && !mbar_wait_bounded(&full[i % NST], (i / NST) & 1, a.st)) dead = true;
+  };
+  auto release = [&](int i) {  // hand stage i % NST back to the producer
+    if (lane == 0)
+      asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&empty[i % NST])) : "memory");
+  };
+  auto k_addr = [&](int i) -> uint32_t {
+    return smem_u32(stages + size_t(i % NST) * STAGE + h * (DK_P * DK_D * 2));
+  };
+  auto zero_tail = [&](int i, int valid) {  // never let the unwritten tail of a last page reach P.V
+    unsigned char* vt = stages + size_t(i % NST) * STAGE + PAGE + h * (DK_P * DK_D * 2);
+    for (int r = valid * 8 + lane; r < DK_P * 8; r += 32)
+      reinterpret_cast<uint4*>(vt)[r] = make_uint4(0u, 0u, 0u, 0u);
+    __syncwarp();
+  };
 
   uint32_t qb[4][2], qn[4][2];
-  float o[4][4];
-  float m0 = -1e30f, m1 = -1e30f, l0 = 0.f, l1 = 0.f;
-  int cur_seq = -1, nxt_seq = -1;
-  bool seen_first = false, dead = false;
-  int64_t seq_fa = 0, seq_fb = 0;
-  const int first_seq = desc_at(0).y >> 7;
-
+  int nxt_seq = -1;
+  const int first_seq = dfirst.y >> 7;  // its piece (if split) uses partial slot 0
   const int k_tok = (lane & 7) + ((lane >> 3) & 1) * 8, k_chk = lane >> 4;
   const int v_tok = (lane & 7) + (lane >> 4) * 8, v_chk = (lane >> 3) & 1;
 
-  for (int i = 0; i < R; ++i) {
-    slide(i);
-    const int2 d = desc_at(i);
+  int i = 0;
+  while (i < R) {
+    slide_to(i);
+    const int4 d = desc_at(i);
     const int seq = d.y >> 7;
-    const bool is_first = (d.y >> 6) & 1, is_last = (d.y >> 5) & 1;
-    const int valid = d.y & 31;
-    const int st = i % NST;
-    unsigned char* kt = stages + size_t(st) * STAGE + h * (DK_P * DK_D * 2);
-    unsigned char* vt = kt + PAGE;
-    if (!dead && !mbar_wait_bounded(&full[st], (i / NST) & 1, a.st)) dead = true;
-
-    if (seq < 0 || seq >= a.n_seqs || valid < 1 || valid > DK_P) {
-      // a page of a sequence the plan rejected: release the stage, compute nothing
+    if (seq < 0 || seq >= a.n_seqs || (d.y & 31) < 1 || (d.y & 31) > DK_P) {
+      // a page of a sequence the plan rejected: drain and release its stage
       if (lane == 0 && !dead) flag(a.st, PKV_DEV_META_BAD);
+      wait_full(i);
       __syncwarp();
-      if (lane == 0) asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&empty[st])) : "memory");
+      release(i);
+      ++i;
       continue;
     }
-    if (seq != cur_seq) {
-      if (seq == nxt_seq) {
+    // this sequence's piece: processing steps [i, i + n)
+    const bool seen_first = (d.y >> 6) & 1;
+    const int n = int(min(int64_t(d.w), seg_end(i)) - pos(i));
+    const bool ends_here = d.w <= p1;
+    if (seq == nxt_seq) {
 #pragma unroll
-        for (int ks = 0; ks < 4; ++ks) { qb[ks][0] = qn[ks][0]; qb[ks][1] = qn[ks][1]; }
+      for (int ks = 0; ks < 4; ++ks) { qb[ks][0] = qn[ks][0]; qb[ks][1] = qn[ks][1]; }
+    } else {
+      load_q_frag<T, GROUPS>(q, seq, a.n_heads, h, g, c4, qb);
+    }
+    // the sequence processed next: H's after T, then each M in turn
+    nxt_seq = (i < lenT) ? (dfirst.y >> 7) : seq + 1;
+    if (nxt_seq < a.n_seqs) load_q_frag<T, GROUPS>(q, nxt_seq, a.n_heads, h, g, c4, qn);
+    float o[4][4];
+#pragma unroll
+    for (int mt = 0; mt < 4; ++mt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) o[mt][e] = 0.f;
+    float m0 = -1e30f, m1 = -1e30f, l0 = 0.f, l1 = 0.f;
+
+    for (int j = 0; j < n; j += DK_U) {
+      const int cnt = min(DK_U, n - j);
+      slide_to(i + j);
+      const int valid = (j + cnt == n && ends_here) ? (desc_at(i + j + cnt - 1).y & 31) : DK_P;
+      if (cnt == DK_U) {
+        uint32_t kb[DK_U], vb[DK_U];
+#pragma unroll
+        for (int u = 0; u < DK_U; ++u) {
+          wait_full(i + j + u);
+          kb[u] = k_addr(i + j + u);
+          vb[u] = kb[u] + PAGE;
+        }
+        if (valid < DK_P) zero_tail(i + j + DK_U - 1, valid);
+        attend_pages<T, DK_U>(kb, vb, valid, qb, o, m0, m1, l0, l1, a.scale_log2, k_tok, k_chk,
+                              v_tok, v_chk, g);
       } else {
-        load_q_frag<T, GROUPS>(q, seq, a.n_heads, h, g, c4, qb);
+        for (int u = 0; u < cnt; ++u) {
+          wait_full(i + j + u);
+          const uint32_t kb[1] = {k_addr(i + j + u)};
+          const uint32_t vb[1] = {kb[0] + PAGE};
+          const int vu = (u == cnt - 1) ? valid : DK_P;
+          if (vu < DK_P) zero_tail(i + j + u, vu);
+          attend_pages<T, 1>(kb, vb, vu, qb, o, m0, m1, l0, l1, a.scale_log2, k_tok, k_chk, v_tok,
+                             v_chk, g);
+        }
       }
-      cur_seq = seq;
-      nxt_seq = seq + 1;
-      seq_fa = a.kv_indptr[seq];  // needed only if the sequence ends split
-      seq_fb = a.kv_indptr[seq + 1];
-      if (nxt_seq < a.n_seqs) load_q_frag<T, GROUPS>(q, nxt_seq, a.n_heads, h, g, c4, qn);
-#pragma unroll
-      for (int mt = 0; mt < 4; ++mt)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) o[mt][e] = 0.f;
-      m0 = m1 = -1e30f;
-      l0 = l1 = 0.f;
-      seen_first = is_first;
-    }
-
-    const bool zeroed = valid < DK_P;
-    if (zeroed) {  // never let the unwritten tail of a last page reach P.V
-      for (int r = valid * 8 + lane; r < DK_P * 8; r += 32)
-        reinterpret_cast<uint4*>(vt)[r] = make_uint4(0u, 0u, 0u, 0u);
       __syncwarp();
+      if (valid < DK_P && lane == 0) fence_proxy_async_smem();  // next TMA lands after the zero stores
+      for (int u = 0; u < cnt; ++u) release(i + j + u);
     }
+    i += n;
 
-    // S^T[16 tok x 8 heads] = K[16 x 64] . Q^T[64 x 8]
-    float s[4] = {0.f, 0.f, 0.f, 0.f}, s2[4] = {0.f, 0.f, 0.f, 0.f};
-    const uint32_t kbase = smem_u32(kt);
-#pragma unroll
-    for (int ks = 0; ks < 4; ++ks) {  // two accumulators halve the dependent mma chain
-      uint32_t af[4];
-      const int chunk = 2 * ks + k_chk;
-      ldsm_x4(af[0], af[1], af[2], af[3], kbase + k_tok * 128 + ((chunk ^ (k_tok & 7)) << 4));
-      MmaOp<T>::run((ks & 1) ? s2 : s, af, qb[ks][0], qb[ks][1]);
-    }
-#pragma unroll
-    for (int e = 0; e < 4; ++e) s[e] += s2[e];
-    // rows g and g+8 are tokens; columns 2*c4, 2*c4+1 are heads of the group
-    const bool v0 = g < valid, v1 = (g + 8) < valid;
-    s[0] = v0 ? s[0] * a.scale_log2 : -INFINITY;
-    s[1] = v0 ? s[1] * a.scale_log2 : -INFINITY;
-    s[2] = v1 ? s[2] * a.scale_log2 : -INFINITY;
-    s[3] = v1 ? s[3] * a.scale_log2 : -INFINITY;
-    float mx0 = fmaxf(s[0], s[2]), mx1 = fmaxf(s[1], s[3]);
-#pragma unroll
-    for (int off = 4; off < 32; off <<= 1) {
-      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
-      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
-    }
-    const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
-    const float al0 = ex2(m0 - mn0), al1 = ex2(m1 - mn1);
-    m0 = mn0;
-    m1 = mn1;
-    const float p00 = ex2(s[0] - mn0), p01 = ex2(s[1] - mn1);
-    const float p10 = ex2(s[2] - mn0), p11 = ex2(s[3] - mn1);
-    l0 = l0 * al0 + p00 + p10;
-    l1 = l1 * al1 + p01 + p11;
-#pragma unroll
-    for (int mt = 0; mt < 4; ++mt) {
-      o[mt][0] *= al0;
-      o[mt][2] *= al0;
-      o[mt][1] *= al1;
-      o[mt][3] *= al1;
-    }
-    const uint32_t pb0 = movmatrix_t(MmaOp<T>::pack(p00, p01));
-    const uint32_t pb1 = movmatrix_t(MmaOp<T>::pack(p10, p11));
-    // O^T[64 dims x 8 heads] += V^T[64 x 16] . P^T[16 x 8]
-    const uint32_t vbase = smem_u32(vt);
-#pragma unroll
-    for (int mt = 0; mt < 4; ++mt) {
-      uint32_t af[4];
-      const int chunk = 2 * mt + v_chk;
-      ldsm_x4_t(af[0], af[1], af[2], af[3], vbase + v_tok * 128 + ((chunk ^ (v_tok & 7)) << 4));
-      MmaOp<T>::run(o[mt], af, pb0, pb1);
-    }
-    __syncwarp();
-    if (lane == 0) {  // release the stage to the producer
-      if (zeroed) fence_proxy_async_smem();  // the next TMA must land after the zero stores
-      asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&empty[st])) : "memory");
-    }
-
-    // end of this sequence within the CTA's range?
-    const bool seq_ends = is_last || (i == R - 1);
-    if (!seq_ends) continue;
+    // finalise the piece: normalise (O/l) into this warp's staging slice
     float lt0 = l0, lt1 = l1;
 #pragma unroll
     for (int off = 4; off < 32; off <<= 1) {
@@ -357,127 +529,62 @@ __global__ void __launch_bounds__(288, MINB) decode_kernel(const __grid_constant
       lt1 += __shfl_xor_sync(0xffffffffu, lt1, off);
     }
     const int j0 = 2 * c4, j1 = 2 * c4 + 1;
-    if (seen_first && is_last) {
-      // the whole sequence lives in this CTA: normalise and store
-      const float i0 = 1.f / lt0, i1 = 1.f / lt1;
+    const float i0 = 1.f / lt0, i1 = 1.f / lt1;
 #pragma unroll
-      for (int mt = 0; mt < 4; ++mt) {
-        const int d0 = mt * 16 + g, d1 = d0 + 8;
-        if (j0 < GROUPS) {
-          ostage[j0 * DK_D + d0] = from_f<T>(o[mt][0] * i0);
-          ostage[j0 * DK_D + d1] = from_f<T>(o[mt][2] * i0);
-        }
-        if (j1 < GROUPS) {
-          ostage[j1 * DK_D + d0] = from_f<T>(o[mt][1] * i1);
-          ostage[j1 * DK_D + d1] = from_f<T>(o[mt][3] * i1);
-        }
+    for (int mt = 0; mt < 4; ++mt) {
+      const int d0 = mt * 16 + g, d1 = d0 + 8;
+      if (j0 < GROUPS) {
+        ostage[j0 * DK_D + d0] = o[mt][0] * i0;
+        ostage[j0 * DK_D + d1] = o[mt][2] * i0;
+      }
+      if (j1 < GROUPS) {
+        ostage[j1 * DK_D + d0] = o[mt][1] * i1;
+        ostage[j1 * DK_D + d1] = o[mt][3] * i1;
+      }
+    }
+    __syncwarp();
+    if (seen_first && ends_here) {
+      // the whole sequence lives in this CTA: store it in the pool dtype
+      T* dst = out + (int64_t(seq) * a.n_heads + h * GROUPS) * DK_D;
+      for (int e = lane * 8; e < GROUPS * DK_D; e += 32 * 8) {
+        const float4 x = *reinterpret_cast<const float4*>(ostage + e);
+        const float4 y = *reinterpret_cast<const float4*>(ostage + e + 4);
+        uint4 v;
+        v.x = MmaOp<T>::pack(x.x, x.y);
+        v.y = MmaOp<T>::pack(x.z, x.w);
+        v.z = MmaOp<T>::pack(y.x, y.y);
+        v.w = MmaOp<T>::pack(y.z, y.w);
+        *reinterpret_cast<uint4*>(dst + e) = v;
       }
       __syncwarp();
-      uint4* dst = reinterpret_cast<uint4*>(out + (int64_t(seq) * a.n_heads + h * GROUPS) * DK_D);
-      for (int ch = lane; ch < GROUPS * 8; ch += 32) dst[ch] = reinterpret_cast<const uint4*>(ostage)[ch];
-      __syncwarp();
-    } else {
-      // a piece of a sequence cut by a range boundary: write (m, l, O/l)
-      const int slot = (seq == first_seq) ? 0 : 1;
-      float* pb = a.partial + (size_t(2 * c + slot) * a.n_heads + h * GROUPS) * (DK_D + 2);
-      const float i0 = 1.f / lt0, i1 = 1.f / lt1;
-#pragma unroll
-      for (int mt = 0; mt < 4; ++mt) {
-        const int d0 = mt * 16 + g, d1 = d0 + 8;
-        if (j0 < GROUPS) {
-          pb[j0 * (DK_D + 2) + d0] = o[mt][0] * i0;
-          pb[j0 * (DK_D + 2) + d1] = o[mt][2] * i0;
-        }
-        if (j1 < GROUPS) {
-          pb[j1 * (DK_D + 2) + d0] = o[mt][1] * i1;
-          pb[j1 * (DK_D + 2) + d1] = o[mt][3] * i1;
-        }
-      }
-      if (g == 0) {
-        if (j0 < GROUPS) { pb[j0 * (DK_D + 2) + DK_D] = m0; pb[j0 * (DK_D + 2) + DK_D + 1] = lt0; }
-        if (j1 < GROUPS) { pb[j1 * (DK_D + 2) + DK_D] = m1; pb[j1 * (DK_D + 2) + DK_D + 1] = lt1; }
-      }
-      cons_sync();  // every consumer warp's piece is written
-      const int64_t fa = seq_fa, fb = seq_fb;
-      const int cf = cta_of(fa, P, G), cl = cta_of(fb - 1, P, G);
-      if (threadIdx.x == 0) {
-        // one acq_rel RMW at gpu scope: releases this CTA's piece (cumulative
-        // over the barrier above) and, for the last CTA, acquires the others'
-        int prev;
-        asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], 1;"
-                     : "=r"(prev) : "l"(a.counters + seq) : "memory");
-        s_last = (prev == cl - cf);
-      }
-      cons_sync();
-      if (s_last) {
-        // merge the pieces: per-head weights first (one pass over (m, l)),
-        // then every output element as one independent sweep over the pieces
-        const int nh = a.n_heads;
-        const int npieces = cl - cf + 1;
-        for (int p0m = 0; p0m < npieces; p0m += DK_MERGE_CHUNK) {
-          const int np = min(DK_MERGE_CHUNK, npieces - p0m);
-          for (int t = threadIdx.x; t < nh; t += n_cons_threads) {
-            float M = -1e30f;
-            for (int k = 0; k < np; ++k) {
-              const int cc = cf + p0m + k;
-              const int sl = (cc == cf && fa > int64_t(cc) * P / G) ? 1 : 0;
-              M = fmaxf(M, __ldcg(a.partial + (size_t(2 * cc + sl) * nh + t) * (DK_D + 2) + DK_D));
-            }
-            if (p0m > 0) M = fmaxf(M, s_mrg_m[t]);
-            float W = 0.f;
-            for (int k = 0; k < np; ++k) {
-              const int cc = cf + p0m + k;
-              const int sl = (cc == cf && fa > int64_t(cc) * P / G) ? 1 : 0;
-              const float* pp = a.partial + (size_t(2 * cc + sl) * nh + t) * (DK_D + 2);
-              const float w = __ldcg(pp + DK_D + 1) * ex2(__ldcg(pp + DK_D) - M);
-              s_mrg_w[k * DK_MERGE_HEADS + t] = w;
-              W += w;
-            }
-            // rescale what earlier chunks accumulated to this chunk's max
-            const float carry = (p0m > 0) ? ex2(s_mrg_m[t] - M) : 0.f;
-            s_mrg_scale[t] = carry;
-            s_mrg_W[t] = (p0m > 0 ? s_mrg_W[t] * carry : 0.f) + W;
-            s_mrg_m[t] = M;
-          }
-          cons_sync();
-          // every thread owns DK_MERGE_PER outputs; all their loads are issued
-          // before any is consumed (one L2 round trip per pass, not one per output)
-          for (int base = 0; base < nh * DK_D; base += n_cons_threads * DK_MERGE_PER) {
-            float acc[DK_MERGE_PER];
-#pragma unroll
-            for (int r = 0; r < DK_MERGE_PER; ++r) {
-              const int idx = base + r * n_cons_threads + threadIdx.x;
-              acc[r] = (p0m > 0 && idx < nh * DK_D) ? s_mrg_acc[idx] * s_mrg_scale[idx / DK_D] : 0.f;
-            }
-            for (int k = 0; k < np; ++k) {
-              const int cc = cf + p0m + k;
-              const int sl = (cc == cf && fa > int64_t(cc) * P / G) ? 1 : 0;
-              const float* pp = a.partial + size_t(2 * cc + sl) * nh * (DK_D + 2);
-              float v[DK_MERGE_PER];
-#pragma unroll
-              for (int r = 0; r < DK_MERGE_PER; ++r) {
-                const int idx = base + r * n_cons_threads + threadIdx.x;
-                v[r] = idx < nh * DK_D ? __ldcg(pp + (idx / DK_D) * (DK_D + 2) + idx % DK_D) : 0.f;
-              }
-#pragma unroll
-              for (int r = 0; r < DK_MERGE_PER; ++r) {
-                const int idx = base + r * n_cons_threads + threadIdx.x;
-                if (idx < nh * DK_D) acc[r] += s_mrg_w[k * DK_MERGE_HEADS + idx / DK_D] * v[r];
-              }
-            }
-#pragma unroll
-            for (int r = 0; r < DK_MERGE_PER; ++r) {
-              const int idx = base + r * n_cons_threads + threadIdx.x;
-              if (idx >= nh * DK_D) continue;
-              const int hh = idx / DK_D, dd = idx % DK_D;
-              if (p0m + np < npieces) s_mrg_acc[idx] = acc[r];
-              else out[(int64_t(seq) * nh + hh) * DK_D + dd] = from_f<T>(acc[r] / s_mrg_W[hh]);
-            }
-          }
-          cons_sync();
-        }
-        if (threadIdx.x == 0) a.counters[seq] = 0;
-      }
+      continue;
+    }
+    // a piece of a sequence cut by a range boundary: publish (O/l, m, l)
+    const int slot = (seq == first_seq) ? 0 : 1;
+    float* po = a.partial_o + (size_t(2 * c + slot) * a.n_heads + h * GROUPS) * DK_D;
+    for (int e = lane * 4; e < GROUPS * DK_D; e += 32 * 4)
+      __stcg(reinterpret_cast<float4*>(po + e), *reinterpret_cast<const float4*>(ostage + e));
+    if (g == 0) {
+      float2* pml = a.partial_ml + size_t(2 * c + slot) * a.n_heads + h * GROUPS;
+      if (j0 < GROUPS) pml[j0] = make_float2(m0, lt0);
+      if (j1 < GROUPS) pml[j1] = make_float2(m1, lt1);
+    }
+    // all consumer warps count the piece in together and, if this CTA completes
+    // the sequence, merge its pieces (a CTA has at most two split pieces)
+    const int n_cons_threads = n_cons * 32;
+    asm volatile("bar.sync 1, %0;" ::"r"(n_cons_threads) : "memory");
+    const int64_t fa = d.z, fb = d.w;
+    const int cf = cta_of(fa, P, G), cl = cta_of(fb - 1, P, G);
+    if (threadIdx.x == 0) {
+      int prev;
+      asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], 1;" : "=r"(prev) : "l"(a.counters + seq) : "memory");
+      s_last = (prev == cl - cf);
+    }
+    asm volatile("bar.sync 1, %0;" ::"r"(n_cons_threads) : "memory");
+    if (s_last) {
+      merge_pieces<T>(a, seq, fa, cf, cl, P, G, threadIdx.x, n_cons_threads, 1, s_ml, s_mrg_W,
+                      s_mrg_M, s_mrg_carry, s_mrg_acc);
+      if (threadIdx.x == 0) a.counters[seq] = 0;
     }
   }
 }
@@ -691,17 +798,17 @@ bool decode_supported(const pkv_pool& p, int n_heads) {
 
 size_t decode_smem(int n_kv_heads, int groups, int nst) {
   const size_t stage = size_t(2) * DK_P * DK_D * 8 * 2;  // K + V page, 8 heads (boxes always 8 wide)
-  return 1024 + nst * stage + bar_bytes(2, nst) + size_t(n_kv_heads) * groups * DK_D * 2;
+  return 1024 + nst * stage + bar_bytes(2, nst) + size_t(n_kv_heads) * groups * DK_D * 4;
 }
 
 // Ring depth and CTAs per SM of the decode kernel. Defaults are the tuned
-// values; PKV_DECODE_NST (2, 3, 4 or 6) and PKV_DECODE_CTAS_PER_SM override them
+// values; PKV_DECODE_NST (3, 4, 5 or 6) and PKV_DECODE_CTAS_PER_SM override them
 // for launch-shape sweeps.
 int decode_nst() {
   static int v = [] {
     const char* e = getenv("PKV_DECODE_NST");
     const int n = e ? atoi(e) : DK_NST;
-    return (n == 2 || n == 3 || n == 4 || n == 6) ? n : DK_NST;
+    return (n == 3 || n == 4 || n == 5 || n == 6) ? n : DK_NST;
   }();
   return v;
 }
@@ -760,10 +867,10 @@ template <typename T, int GROUPS>
 int launch_decode_n(const pkv_pool& p, const CUtensorMap& tm, DecodeArgs& a, int64_t tp,
                     cudaStream_t s) {
   switch (decode_nst()) {
-    case 2: return launch_decode_t<T, GROUPS, 2, 2>(p, tm, a, tp, s);
-    case 3: return launch_decode_t<T, GROUPS, 3, 2>(p, tm, a, tp, s);
-    case 4: return launch_decode_t<T, GROUPS, 4, 1>(p, tm, a, tp, s);
-    default: return launch_decode_t<T, GROUPS, 6, 1>(p, tm, a, tp, s);
+    case 3: return launch_decode_t<T, GROUPS, 3, 1>(p, tm, a, tp, s);
+    case 5: return launch_decode_t<T, GROUPS, 5, 1>(p, tm, a, tp, s);
+    case 6: return launch_decode_t<T, GROUPS, 6, 1>(p, tm, a, tp, s);
+    default: return launch_decode_t<T, GROUPS, 4, 1>(p, tm, a, tp, s);
   }
 }
 
@@ -813,7 +920,7 @@ extern "C" int pkv_plan(const pkv_pool* pool, int32_t n_heads, const pkv_batch* 
   char* ws = static_cast<char*>(workspace);
   // every descriptor starts as "no sequence" (-1): pages of a sequence the
   // plan rejects are skipped by the decode kernel instead of read as garbage
-  PKV_CUDA_RET(cudaMemsetAsync(ws + w.page_desc, 0xff, sizeof(int2) * size_t(batch->total_pages),
+  PKV_CUDA_RET(cudaMemsetAsync(ws + w.page_desc, 0xff, sizeof(int4) * size_t(batch->total_pages),
                                static_cast<cudaStream_t>(stream)));
   const int threads = 256;
   const int64_t n_threads = int64_t(batch->n_seqs) * 32;
@@ -821,7 +928,7 @@ extern "C" int pkv_plan(const pkv_pool* pool, int32_t n_heads, const pkv_batch* 
                 static_cast<cudaStream_t>(stream)>>>(
       batch->kv_indptr, batch->kv_indices, batch->kv_last_page_len, batch->kv_lens,
       batch->cu_query_lens, batch->n_seqs, batch->total_pages, pool->block_size, pool->num_blocks,
-      reinterpret_cast<int2*>(ws + w.page_desc), reinterpret_cast<int32_t*>(ws + w.counters),
+      reinterpret_cast<int4*>(ws + w.page_desc), reinterpret_cast<int32_t*>(ws + w.counters),
       1, batch->dev_status);
   PKV_CUDA_RET(cudaGetLastError());
   return PKV_OK;
@@ -857,8 +964,9 @@ extern "C" int pkv_attend_planned(const pkv_pool* pool, int32_t layer, int32_t n
     a.q = q;
     a.out = out;
     a.kv_indptr = batch->kv_indptr;
-    a.desc = reinterpret_cast<const int2*>(ws + w.page_desc);
-    a.partial = reinterpret_cast<float*>(ws + w.partial);
+    a.desc = reinterpret_cast<const int4*>(ws + w.page_desc);
+    a.partial_o = reinterpret_cast<float*>(ws + w.partial_o);
+    a.partial_ml = reinterpret_cast<float2*>(ws + w.partial_ml);
     a.counters = reinterpret_cast<int32_t*>(ws + w.counters);
     a.st = batch->dev_status;
     a.total_pages = batch->total_pages;

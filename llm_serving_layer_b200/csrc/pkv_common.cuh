@@ -110,6 +110,21 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// As mbar_wait_bounded, for waiters off the critical path (the decode
+// kernel's producer and merge warps): sleeps `ns` between probes so a waiting
+// warp does not take issue slots from the warps doing the work.
+__device__ __forceinline__ bool mbar_wait_bounded_sleepy(uint64_t* bar, uint32_t parity, int32_t* st,
+                                                         unsigned ns) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (globaltimer_ns() - t0 < 1000000000ull) {
+    __nanosleep(ns);
+    if (mbar_try_wait(bar, parity)) return true;
+  }
+  flag(st, PKV_DEV_WAIT_TIMEOUT);
+  return false;
+}
+
 // TMA -----------------------------------------------------------------------
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
