@@ -131,6 +131,28 @@ PKV_API int pkv_attend_planned(const pkv_pool* pool, int32_t layer, int32_t n_he
                        void* out, float scale, const pkv_batch* batch, int32_t decode_hint,
                        void* workspace, size_t workspace_bytes, void* stream);
 
+/* Decode attention that allocates nothing and takes no workspace. No
+ * counterpart in the reference: it is for callers that cannot allocate device
+ * memory — a serving process that gives (nearly) all of HBM to its KV pool and
+ * allocates nothing afterwards, or a host that owns every device allocation
+ * and does not let a plug-in library call cudaMalloc. Same arguments and
+ * result as pkv_attend with decode_hint = 1 (plan + split-K decode kernel), for
+ * the decode kernel's geometry only (fp16/bf16 pool, head_dim 64, 16-token
+ * pages, <= 8 KV heads, 1/2/4/8 query heads per KV head; PKV_ERR_UNSUPPORTED
+ * otherwise).
+ * Scratch: one file-scope 8 MiB device array, held by every GPU that loads
+ * the library until the process exits; a batch needing more (about 340k pages
+ * at 32 query heads, 190k at 64,
+ * or very many sequences) is rejected with PKV_ERR_ARG. The first call on a
+ * device looks up the array's device address (cudaGetSymbolAddress); make that
+ * first call before any stream capture. Every call shares the array and leaves
+ * its contents behind (each call re-initialises what it reads), so calls that
+ * overlap on the GPU — on different streams, or from different threads —
+ * race and must be serialised by the caller. Calls no cudaMalloc / cudaFree. */
+PKV_API int pkv_attend_decode_noalloc(const pkv_pool* pool, int32_t layer, int32_t n_heads,
+                                      const void* q, void* out, float scale,
+                                      const pkv_batch* batch, void* stream);
+
 /* ---- copy-on-write ---------------------------------------------------------
  * Replaces PagedTorchBackend.copy_block (serving/backends/paged_torch.py:181-207)
  * and FlashInferBackend.copy_block (flashinfer_backend.py:415-441), batched:

@@ -1023,3 +1023,128 @@ extern "C" int pkv_attend(const pkv_pool* pool, int32_t layer, int32_t n_heads, 
   return pkv_attend_planned(pool, layer, n_heads, q, out, scale, batch, decode_hint, workspace,
                             workspace_bytes, stream);
 }
+
+// ---------------------------------------------------------------- no-allocation decode
+//
+// pkv_attend_decode_noalloc: the decode path (plan + split-K decode kernel) for
+// callers that cannot allocate device memory — a serving process that hands
+// (nearly) all of HBM to its own KV pool and allocates nothing afterwards, or a
+// host that owns every device allocation and does not let a plug-in library
+// call cudaMalloc. The per-step scratch (page descriptors, split-K counters and
+// partials) lives in one file-scope __device__ array instead of a caller's
+// workspace.
+
+namespace pkv {
+namespace {
+
+// Bytes of the shared scratch: split-K partials for 148 CTAs plus one 16-byte
+// descriptor per page leave room for ~340k pages at 32 query heads (~190k at
+// 64). Every GPU that loads the library holds this array until the process exits.
+constexpr size_t NOALLOC_SCRATCH_BYTES = size_t(8) << 20;
+__device__ __align__(256) unsigned char g_noalloc_scratch[NOALLOC_SCRATCH_BYTES];
+
+// Device address of g_noalloc_scratch for the current device. The host-side
+// symbol is only a stand-in, never a device address: the address is looked up
+// once per device (with that device current) and cached.
+int noalloc_scratch(void** out) {
+  static std::mutex mu;
+  static std::vector<void*> addr;
+  int dev = 0;
+  PKV_CUDA_RET(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lock(mu);
+  if ((int)addr.size() <= dev) addr.resize(dev + 1, nullptr);
+  if (!addr[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || !p) return cuda_fail(e, "cudaGetSymbolAddress(g_noalloc_scratch)");
+    addr[dev] = p;
+  }
+  *out = addr[dev];
+  return PKV_OK;
+}
+
+// Upper bound of the decode kernel's grid for this pool (the same occupancy
+// query the launch uses), so the scratch layout covers every CTA's partials.
+template <typename T, int GROUPS>
+int decode_grid_cap_n(const pkv_pool& p) {
+  switch (decode_nst()) {
+    case 3: return decode_grid_limit<T, GROUPS, 3, 1>(p.n_kv_heads);
+    case 5: return decode_grid_limit<T, GROUPS, 5, 1>(p.n_kv_heads);
+    case 6: return decode_grid_limit<T, GROUPS, 6, 1>(p.n_kv_heads);
+    default: return decode_grid_limit<T, GROUPS, 4, 1>(p.n_kv_heads);
+  }
+}
+template <typename T>
+int decode_grid_cap(const pkv_pool& p, int groups) {
+  switch (groups) {
+    case 1: return decode_grid_cap_n<T, 1>(p);
+    case 2: return decode_grid_cap_n<T, 2>(p);
+    case 4: return decode_grid_cap_n<T, 4>(p);
+    default: return decode_grid_cap_n<T, 8>(p);
+  }
+}
+
+}  // namespace
+}  // namespace pkv
+
+extern "C" int pkv_attend_decode_noalloc(const pkv_pool* pool, int32_t layer, int32_t n_heads,
+                                         const void* q, void* out, float scale,
+                                         const pkv_batch* batch, void* stream) {
+  if (int rc = check_pool(pool)) return rc;
+  const pkv_pool& p = *pool;
+  if (layer < 0 || layer >= p.num_layers)
+    return fail(PKV_ERR_ARG, "layer_idx " + std::to_string(layer) + " out of range [0, " +
+                                 std::to_string(p.num_layers) + ")");
+  if (int rc = check_batch(p, n_heads, batch)) return rc;
+  if (!q || !out) return fail(PKV_ERR_ARG, "q and out must be non-NULL");
+  if (!decode_supported(p, n_heads))
+    return fail(PKV_ERR_UNSUPPORTED, "no-allocation decode needs an fp16/bf16 pool, head_dim 64, "
+                                     "16-token pages, <= 8 KV heads and 1/2/4/8 query heads per KV head");
+  if (batch->n_tokens != batch->n_seqs)
+    return fail(PKV_ERR_ARG, "decode: n_tokens must equal n_seqs (one query per sequence)");
+  if (batch->total_pages == 0) return fail(PKV_ERR_ARG, "decode: empty page table");
+  if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(out)) & 15)
+    return fail(PKV_ERR_ARG, "q and out must be 16-byte aligned");
+  const int groups = n_heads / p.n_kv_heads;
+  const int cap = p.dtype == PKV_F16 ? decode_grid_cap<__half>(p, groups)
+                                     : decode_grid_cap<__nv_bfloat16>(p, groups);
+  if (cap <= 0) return PKV_ERR_CUDA;  // message already set
+  const WsLayout w = ws_layout(n_heads, batch->n_seqs, batch->total_pages,
+                               std::min(cap, max_decode_grid()), p.head_dim);
+  if (w.total > NOALLOC_SCRATCH_BYTES)
+    return fail(PKV_ERR_ARG, "batch needs " + std::to_string(w.total) + " bytes of scratch; the "
+                             "no-allocation decode has " + std::to_string(NOALLOC_SCRATCH_BYTES) +
+                             " (fewer pages or sequences per call, or use pkv_attend with a workspace)");
+  void* scratch = nullptr;
+  if (int rc = noalloc_scratch(&scratch)) return rc;
+  char* ws = static_cast<char*>(scratch);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // plan: descriptors start at -1, counters are zeroed by the plan kernel, so
+  // nothing left in the shared scratch by an earlier call is read
+  PKV_CUDA_RET(cudaMemsetAsync(ws + w.page_desc, 0xff, sizeof(int4) * size_t(batch->total_pages), s));
+  const int64_t n_threads = int64_t(batch->n_seqs) * 32;
+  plan_kernel<<<unsigned((n_threads + 255) / 256), 256, 0, s>>>(
+      batch->kv_indptr, batch->kv_indices, batch->kv_last_page_len, batch->kv_lens,
+      batch->cu_query_lens, batch->n_seqs, batch->total_pages, p.block_size, p.num_blocks,
+      reinterpret_cast<int4*>(ws + w.page_desc), reinterpret_cast<int32_t*>(ws + w.counters), 1,
+      batch->dev_status);
+  PKV_CUDA_RET(cudaGetLastError());
+  CUtensorMap tm;
+  if (int rc = get_tmap(p, &tm)) return rc;
+  DecodeArgs a;
+  a.q = q;
+  a.out = out;
+  a.kv_indptr = batch->kv_indptr;
+  a.desc = reinterpret_cast<const int4*>(ws + w.page_desc);
+  a.partial_o = reinterpret_cast<float*>(ws + w.partial_o);
+  a.partial_ml = reinterpret_cast<float2*>(ws + w.partial_ml);
+  a.counters = reinterpret_cast<int32_t*>(ws + w.counters);
+  a.st = batch->dev_status;
+  a.total_pages = batch->total_pages;
+  a.n_seqs = batch->n_seqs;
+  a.n_heads = n_heads;
+  a.layer = layer;
+  a.scale_log2 = scale * 1.4426950408889634f;
+  if (p.dtype == PKV_F16) return launch_decode_g<__half>(p, groups, tm, a, batch->total_pages, s);
+  return launch_decode_g<__nv_bfloat16>(p, groups, tm, a, batch->total_pages, s);
+}
