@@ -110,7 +110,11 @@ PKV_API int pkv_append_kv(const pkv_pool* pool, int32_t layer, const void* k, co
  * q, out: device [n_tokens][n_heads][head_dim] in the pool dtype.
  *
  * `decode_hint` != 0 selects the split-K decode kernel, which requires every
- * query length to be 1 (checked on the device: PKV_DEV_QLEN_BAD). Workspace
+ * query length to be 1 (checked on the device: PKV_DEV_QLEN_BAD). Otherwise a
+ * batch with n_tokens != n_seqs (chunked prefill, prefill mixed with decode
+ * tokens) runs the tensor-core prefill kernel when the geometry allows (the
+ * decode kernel's: fp16/bf16, head_dim 64, 16-token pages, <= 8 KV heads,
+ * 1/2/4/8 query heads per KV head), else the generic kernel. Workspace
  * (device, 256-byte aligned) of at least pkv_attend_workspace_size() bytes must
  * be given; its counters must be zero before the first call on it and are left
  * zero by every call. */
@@ -120,16 +124,30 @@ PKV_API int pkv_attend(const pkv_pool* pool, int32_t layer, int32_t n_heads, con
                float scale, const pkv_batch* batch, int32_t decode_hint, void* workspace,
                size_t workspace_bytes, void* stream);
 
-/* Build the per-step page schedule the decode kernel reads (once per step,
- * reused by every layer's pkv_attend with the same batch and workspace). Also
- * validates the CSR on the device (PKV_DEV_META_BAD / PKV_DEV_SLOT_OOB /
- * PKV_DEV_QLEN_BAD). pkv_attend is pkv_plan (decode only) followed by
- * pkv_attend_planned; a caller attending every layer of one step plans once. */
+/* Build the per-step schedule the attention kernels read (once per step,
+ * reused by every layer's pkv_attend_planned with the same batch and
+ * workspace): for n_tokens == n_seqs the decode kernel's page descriptors
+ * (validating the CSR on the device: PKV_DEV_META_BAD / PKV_DEV_SLOT_OOB /
+ * PKV_DEV_QLEN_BAD), otherwise the prefill kernel's tile list, longest tiles
+ * first (nothing when only the generic kernel takes the batch). pkv_attend is
+ * pkv_plan followed by pkv_attend_planned; a caller attending every layer of
+ * one step plans once. The workspace size for a non-decode step is
+ * pkv_attend_workspace_size(..., decode_hint = 0). */
 PKV_API int pkv_plan(const pkv_pool* pool, int32_t n_heads, const pkv_batch* batch, void* workspace,
              size_t workspace_bytes, void* stream);
 PKV_API int pkv_attend_planned(const pkv_pool* pool, int32_t layer, int32_t n_heads, const void* q,
                        void* out, float scale, const pkv_batch* batch, int32_t decode_hint,
                        void* workspace, size_t workspace_bytes, void* stream);
+
+/* Which kernel pkv_attend_planned runs for a batch of this shape and hint
+ * (host only, nothing touches the device): PKV_KERNEL_GENERIC,
+ * PKV_KERNEL_DECODE or PKV_KERNEL_PREFILL; -PKV_ERR_ARG for a bad pool. No
+ * counterpart in the reference (its backends have one code path each). */
+#define PKV_KERNEL_GENERIC 0
+#define PKV_KERNEL_DECODE 1
+#define PKV_KERNEL_PREFILL 2
+PKV_API int pkv_attend_kernel(const pkv_pool* pool, int32_t n_heads, int32_t n_seqs, int32_t n_tokens,
+                      int32_t decode_hint);
 
 /* Decode attention that allocates nothing and takes no workspace. No
  * counterpart in the reference: it is for callers that cannot allocate device

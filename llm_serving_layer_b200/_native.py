@@ -17,6 +17,8 @@ import torch
 LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libpkv.so"
 
 PKV_OK, PKV_ERR_ARG, PKV_ERR_UNSUPPORTED, PKV_ERR_CUDA, PKV_ERR_DEVICE = 0, 1, 2, 3, 4
+PKV_KERNEL_GENERIC, PKV_KERNEL_DECODE, PKV_KERNEL_PREFILL = 0, 1, 2
+KERNEL_NAMES = {PKV_KERNEL_GENERIC: "generic", PKV_KERNEL_DECODE: "decode", PKV_KERNEL_PREFILL: "prefill"}
 DEV_SLOT_OOB, DEV_META_BAD, DEV_QLEN_BAD, DEV_WAIT_TIMEOUT, DEV_WORKSPACE = 0x1, 0x2, 0x4, 0x8, 0x10
 
 DTYPE_CODE = {torch.float16: 0, torch.bfloat16: 1, torch.float32: 2, torch.float64: 3}
@@ -49,6 +51,7 @@ SIGNATURES = {
     "pkv_attend": (c_i32, [P_POOL, c_i32, c_i32, c_vp, c_vp, c_float, P_BATCH, c_i32, c_vp, c_size, c_vp]),
     "pkv_plan": (c_i32, [P_POOL, c_i32, P_BATCH, c_vp, c_size, c_vp]),
     "pkv_attend_planned": (c_i32, [P_POOL, c_i32, c_i32, c_vp, c_vp, c_float, P_BATCH, c_i32, c_vp, c_size, c_vp]),
+    "pkv_attend_kernel": (c_i32, [P_POOL, c_i32, c_i32, c_i32, c_i32]),
     "pkv_attend_decode_noalloc": (c_i32, [P_POOL, c_i32, c_i32, c_vp, c_vp, c_float, P_BATCH, c_vp]),
     "pkv_copy_blocks": (c_i32, [P_POOL, c_vp, c_vp, c_i64, c_vp, c_vp]),
     "pkv_copy_block": (c_i32, [P_POOL, c_i64, c_i64, c_vp]),

@@ -107,6 +107,7 @@ class B200PagedBackend:
         self._meta_state: dict[str, Any] = {}
         self.n_plans = 0
         self.n_runs = 0
+        self.last_kernel: str | None = None  # "decode" | "prefill" | "generic": kernel of the last attend
 
     # -- accounting (paged_torch.py:139-177) ----------------------------------
 
@@ -222,6 +223,7 @@ class B200PagedBackend:
         if tokens == 0:
             return out
         self.n_runs += 1
+        self.last_kernel = st["kernel"]
         N.check(self._lib.pkv_attend_planned(
             self._pdesc, layer_idx, self.n_heads, q.data_ptr(), out.data_ptr(), float(scale),
             ctypes.byref(st["batch"]), int(st["decode"]), st["ws_ptr"], st["ws_bytes"],
@@ -280,13 +282,16 @@ class B200PagedBackend:
         if self._ws is None or self._ws.numel() < need:
             self._ws = torch.zeros(max(need, 1 << 20), dtype=torch.uint8, device=self.device)
         ws_ptr, ws_bytes = self._ws.data_ptr(), self._ws.numel()
-        if decode and n_tokens > 0:
+        kernel = int(self._lib.pkv_attend_kernel(self._pdesc, self.n_heads, n, n_tokens, int(decode)))
+        if kernel < 0:
+            N.check(-kernel, "attend")
+        if n_tokens > 0 and (decode or kernel == N.PKV_KERNEL_PREFILL):
             N.check(self._lib.pkv_plan(self._pdesc, self.n_heads, ctypes.byref(batch), ws_ptr, ws_bytes,
                                        N.stream_ptr(self.device)), "plan")
             self.n_plans += 1
         self._meta = meta
         self._meta_state = {"batch": batch, "tensors": t, "decode": decode, "n_tokens": n_tokens,
-                            "ws_ptr": ws_ptr, "ws_bytes": ws_bytes}
+                            "ws_ptr": ws_ptr, "ws_bytes": ws_bytes, "kernel": N.KERNEL_NAMES[kernel]}
         return self._meta_state
 
     def _host_validate(self, meta: Any, n: int, total_pages: int) -> bool:

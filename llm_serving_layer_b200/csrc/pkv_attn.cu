@@ -48,12 +48,17 @@ struct WsLayout {
   size_t counters = 0;   // int32[n_seqs]
   size_t partial_o = 0;   // float[2 * grid][n_heads][D]
   size_t partial_ml = 0;  // float2[2 * grid][n_heads]
+  size_t n_tiles = 0;     // int32: prefill tiles planned (prefill layout only)
+  size_t tiles = 0;       // int2[tiles_cap] {seq, first token} (prefill layout only)
   size_t total = 0;
 };
 
 inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
-WsLayout ws_layout(int n_heads, int n_seqs, int64_t total_pages, int max_grid, int head_dim) {
+// tiles_cap > 0 appends the prefill tile list after the decode regions (whose
+// offsets do not depend on it).
+WsLayout ws_layout(int n_heads, int n_seqs, int64_t total_pages, int max_grid, int head_dim,
+                   int64_t tiles_cap = 0) {
   WsLayout w;
   size_t off = 0;
   w.page_desc = off;
@@ -64,6 +69,12 @@ WsLayout ws_layout(int n_heads, int n_seqs, int64_t total_pages, int max_grid, i
   off = align256(off + sizeof(float) * size_t(2) * max_grid * n_heads * head_dim);
   w.partial_ml = off;
   off = align256(off + sizeof(float2) * size_t(2) * max_grid * n_heads);
+  if (tiles_cap > 0) {
+    w.n_tiles = off;
+    off = align256(off + sizeof(int32_t));
+    w.tiles = off;
+    off = align256(off + sizeof(int2) * size_t(tiles_cap));
+  }
   w.total = off;
   return w;
 }
@@ -898,26 +909,42 @@ int check_batch(const pkv_pool& p, int32_t n_heads, const pkv_batch* b) {
   return PKV_OK;
 }
 
+// Workspace layout of a step: the decode regions, plus the prefill tile list
+// when the step is not a decode step and the prefill kernel takes it.
+WsLayout step_layout(const pkv_pool* pool, int n_heads, int n_seqs, int64_t total_pages, bool decode) {
+  const int d = pool ? pool->head_dim : DK_D;
+  const int64_t cap = (!decode && pool && prefill_supported(*pool, n_heads))
+                          ? prefill_tiles_cap(n_seqs, total_pages) : 0;
+  return ws_layout(n_heads, n_seqs, total_pages, max_decode_grid(), d, cap);
+}
+
 }  // namespace
+
+int pool_tmap(const pkv_pool& p, CUtensorMap* out) { return get_tmap(p, out); }
+
 }  // namespace pkv
 
 using namespace pkv;
 
 extern "C" size_t pkv_attend_workspace_size(const pkv_pool* pool, int32_t n_heads, int32_t n_seqs,
                                             int64_t total_pages, int32_t decode_hint) {
-  (void)decode_hint;
-  const int d = pool ? pool->head_dim : DK_D;
-  return ws_layout(n_heads, n_seqs, total_pages, max_decode_grid(), d).total;
+  return step_layout(pool, n_heads, n_seqs, total_pages, decode_hint != 0).total;
 }
 
 extern "C" int pkv_plan(const pkv_pool* pool, int32_t n_heads, const pkv_batch* batch,
                         void* workspace, size_t workspace_bytes, void* stream) {
   if (int rc = check_pool(pool)) return rc;
   if (int rc = check_batch(*pool, n_heads, batch)) return rc;
-  const WsLayout w = ws_layout(n_heads, batch->n_seqs, batch->total_pages, max_decode_grid(), pool->head_dim);
+  const bool decode = batch->n_tokens == batch->n_seqs;
+  if (!decode && !prefill_supported(*pool, n_heads)) return PKV_OK;  // the generic kernel needs no plan
+  const WsLayout w = step_layout(pool, n_heads, batch->n_seqs, batch->total_pages, decode);
   if (!workspace || workspace_bytes < w.total)
     return fail(PKV_ERR_ARG, "workspace too small: need " + std::to_string(w.total) + " bytes");
   char* ws = static_cast<char*>(workspace);
+  if (!decode)
+    return prefill_plan(*pool, n_heads, *batch, reinterpret_cast<int2*>(ws + w.tiles),
+                        reinterpret_cast<int32_t*>(ws + w.n_tiles), prefill_tiles_cap(batch->n_seqs, batch->total_pages),
+                        static_cast<cudaStream_t>(stream));
   // every descriptor starts as "no sequence" (-1): pages of a sequence the
   // plan rejects are skipped by the decode kernel instead of read as garbage
   PKV_CUDA_RET(cudaMemsetAsync(ws + w.page_desc, 0xff, sizeof(int4) * size_t(batch->total_pages),
@@ -952,7 +979,7 @@ extern "C" int pkv_attend_planned(const pkv_pool* pool, int32_t layer, int32_t n
     if (batch->n_tokens != batch->n_seqs)
       return fail(PKV_ERR_ARG, "decode: n_tokens must equal n_seqs (one query per sequence)");
     if (batch->total_pages == 0) return fail(PKV_ERR_ARG, "decode: empty page table");
-    const WsLayout w = ws_layout(n_heads, batch->n_seqs, batch->total_pages, max_decode_grid(), p.head_dim);
+    const WsLayout w = step_layout(pool, n_heads, batch->n_seqs, batch->total_pages, true);
     if (!workspace || workspace_bytes < w.total)
       return fail(PKV_ERR_ARG, "workspace too small: need " + std::to_string(w.total) + " bytes");
     if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(out)) & 15)
@@ -977,6 +1004,16 @@ extern "C" int pkv_attend_planned(const pkv_pool* pool, int32_t layer, int32_t n
     const int groups = n_heads / p.n_kv_heads;
     if (p.dtype == PKV_F16) return launch_decode_g<__half>(p, groups, tm, a, batch->total_pages, s);
     return launch_decode_g<__nv_bfloat16>(p, groups, tm, a, batch->total_pages, s);
+  }
+
+  if (!decode_hint && batch->n_tokens != batch->n_seqs && prefill_supported(p, n_heads)) {
+    const WsLayout w = step_layout(pool, n_heads, batch->n_seqs, batch->total_pages, false);
+    if (!workspace || workspace_bytes < w.total)
+      return fail(PKV_ERR_ARG, "workspace too small: need " + std::to_string(w.total) + " bytes");
+    char* ws = static_cast<char*>(workspace);
+    return prefill_attend(p, layer, n_heads, q, out, scale, *batch, reinterpret_cast<const int2*>(ws + w.tiles),
+                          reinterpret_cast<const int32_t*>(ws + w.n_tiles),
+                          prefill_tiles_cap(batch->n_seqs, batch->total_pages), s);
   }
 
   if (p.head_dim > 32 * GEN_MAX_DPL)
@@ -1014,10 +1051,20 @@ extern "C" int pkv_attend_planned(const pkv_pool* pool, int32_t layer, int32_t n
   return PKV_OK;
 }
 
+extern "C" int pkv_attend_kernel(const pkv_pool* pool, int32_t n_heads, int32_t n_seqs, int32_t n_tokens,
+                                 int32_t decode_hint) {
+  if (int rc = check_pool(pool)) return -rc;
+  if (n_heads <= 0 || n_heads % pool->n_kv_heads) return -fail(PKV_ERR_ARG, "n_heads must be a positive multiple of n_kv_heads");
+  if (decode_hint && decode_supported(*pool, n_heads)) return PKV_KERNEL_DECODE;
+  if (!decode_hint && n_tokens != n_seqs && prefill_supported(*pool, n_heads)) return PKV_KERNEL_PREFILL;
+  return PKV_KERNEL_GENERIC;
+}
+
 extern "C" int pkv_attend(const pkv_pool* pool, int32_t layer, int32_t n_heads, const void* q,
                           void* out, float scale, const pkv_batch* batch, int32_t decode_hint,
                           void* workspace, size_t workspace_bytes, void* stream) {
-  if (decode_hint && pool && decode_supported(*pool, n_heads)) {
+  if (pool && batch && ((decode_hint && decode_supported(*pool, n_heads)) ||
+                        (!decode_hint && batch->n_tokens != batch->n_seqs && prefill_supported(*pool, n_heads)))) {
     if (int rc = pkv_plan(pool, n_heads, batch, workspace, workspace_bytes, stream)) return rc;
   }
   return pkv_attend_planned(pool, layer, n_heads, q, out, scale, batch, decode_hint, workspace,

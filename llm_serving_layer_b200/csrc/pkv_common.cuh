@@ -48,6 +48,21 @@ inline int64_t slab_bytes(const pkv_pool& p) { return block_bytes(p) * p.num_blo
 
 int num_sms();  // SM count of the current device (cached per device)
 
+// Tensor map of a pool's permuted page view (dims D, token slot, KV head,
+// layer*2+kv; one box = one whole [8 heads][16 tok][64] page of one layer's K
+// or V), cached per (device, pool). pkv_attn.cu.
+int pool_tmap(const pkv_pool& p, CUtensorMap* out);
+
+// Chunked-prefill / mixed-batch tensor-core attention (pkv_prefill.cu).
+bool prefill_supported(const pkv_pool& p, int n_heads);
+int prefill_tile_tokens(int n_heads, int n_kv_heads);
+int64_t prefill_tiles_cap(int n_seqs, int64_t total_pages);
+int prefill_plan(const pkv_pool& p, int n_heads, const pkv_batch& b, int2* tiles, int32_t* n_tiles,
+                 int64_t tiles_cap, cudaStream_t s);
+int prefill_attend(const pkv_pool& p, int layer, int n_heads, const void* q, void* out, float scale,
+                   const pkv_batch& b, const int2* tiles, const int32_t* n_tiles, int64_t tiles_cap,
+                   cudaStream_t s);
+
 // ---------------------------------------------------------------- device side
 __device__ __forceinline__ void flag(int32_t* st, int32_t bits) {
   if (st) atomicOr(st, bits);
