@@ -381,6 +381,9 @@ def run_b200(args) -> None:
     # ---- swap (config 4), rank 0 measures its own GPU's host link
     if args.swap and rank == 0:
         line_extra["swap"] = run_swap(torch, bk, args, device)
+    # ---- chunked prefill with radix sharing (config 3), rank 0
+    if args.prefill and rank == 0:
+        line_extra["prefill"] = run_prefill(torch, bk, args, device)
     if ws > 1:
         dist.barrier()
 
@@ -478,6 +481,250 @@ def run_e2e(torch, bk, tables, ctx, args, device, ws, dist, n_graphs) -> dict:
             "path": "B200PagedBackend.append_kv/attend per layer, validate='device', host BatchMeta built per step"}
 
 
+def prefill_workload(seed: int):
+    """Config 3: 512 prompts, lengths U[128, 1024], in 32 families sharing a
+    prefix of U[64, 512] tokens. Each family's first prompt (its owner) is
+    prefilled in full; every later member references the owner's whole prefix
+    blocks and copies the partial last prefix block on its first write
+    (copy-on-write), then prefills from the end of the prefix. Prompts are cut
+    into steps of at most 512 prompt tokens across the batch, each prompt
+    contributing one contiguous range per step (the reference scheduler's
+    max_prefill_tokens = 512). Returns per-step (prompt ids, starts, ends),
+    the block tables, the copy-on-write pairs per step and summary counts."""
+    rs = np.random.RandomState(seed)
+    n_fam, per_fam, budget = 32, 16, 512
+    pf = rs.randint(64, 513, size=n_fam)
+    lens, fam = [], []
+    for f in range(n_fam):
+        for _ in range(per_fam):
+            lens.append(int(rs.randint(max(128, int(pf[f]) + 1), 1025)))
+            fam.append(f)
+    owners = [f * per_fam for f in range(n_fam)]
+    members = [i for i in range(n_fam * per_fam) if i % per_fam]
+    order = owners + [members[j] for j in rs.permutation(len(members))]
+    free = list(rs.permutation(1 << 20))  # block ids drawn from a scattered free list (trimmed to the pool later)
+    nxt = 0
+    tables, start, cow = {}, {}, {}
+    for i in order:
+        f, L_i = fam[i], lens[i]
+        nb = (L_i + P - 1) // P
+        if i in owners:
+            tables[i] = free[nxt:nxt + nb]
+            nxt += nb
+            start[i] = 0
+        else:
+            own = tables[owners[f]]
+            whole = int(pf[f]) // P
+            t = list(own[:whole])
+            if pf[f] % P:
+                new = free[nxt]
+                nxt += 1
+                cow[i] = (own[whole], new)
+                t.append(new)
+            rest = nb - len(t)
+            t += free[nxt:nxt + rest]
+            nxt += rest
+            tables[i] = t
+            start[i] = int(pf[f])
+    steps, cows, pos = [], [], {i: start[i] for i in order}
+    queue = list(order)
+    while queue:
+        left, ids, st, en, cw = budget, [], [], [], []
+        k = 0
+        while left > 0 and k < len(queue):
+            i = queue[k]
+            take = min(left, lens[i] - pos[i])
+            if pos[i] == start[i] and i in cow:
+                cw.append(cow[i])
+            ids.append(i)
+            st.append(pos[i])
+            en.append(pos[i] + take)
+            pos[i] += take
+            left -= take
+            k += 1
+        queue = [i for i in queue if pos[i] < lens[i]]
+        steps.append((ids, st, en))
+        cows.append(cw)
+    total_blocks = sum((l + P - 1) // P for l in lens)
+    shared = sum(int(pf[fam[i]]) // P for i in members)
+    return {"steps": steps, "tables": tables, "cows": cows, "blocks_used": nxt,
+            "prompt_tokens": sum(lens), "computed_tokens": sum(lens[i] - start[i] for i in order),
+            "block_reuse": shared / total_blocks, "n_cow": len(cow)}
+
+
+def prefill_step_work(ids, st, en) -> tuple[float, float]:
+    """Algorithmic FLOPs and bytes of one prefill attention launch: FLOPs =
+    4 * Hq * D * unmasked (query, key) pairs, pairs = q*s + q(q+1)/2 per
+    sequence; bytes = K+V of every key read once + Q read + O written."""
+    fl = by = 0.0
+    for s0, e in zip(st, en):
+        q = e - s0
+        fl += 4 * HQ * D * (q * s0 + q * (q + 1) / 2)
+        by += e * HKV * D * 2 * 2 + q * HQ * D * 2 * 2
+    return fl, by
+
+
+def cpu_prefill_time(work: dict, budget_s: float) -> dict:
+    """CPU oracle (reference prefill attend restated in numpy, float32) on the
+    first steps of the config-3 schedule, one layer each, for ~budget_s."""
+    from oracle import attend_reference  # CPU baseline leg only
+    from llm_serving_layer_b200.meta import build_meta
+
+    rs = np.random.RandomState(7)
+    t_end = time.perf_counter() + budget_s
+    toks = secs = 0.0
+    n = 0
+    for ids, st, en in work["steps"]:
+        tabs = [list(range(0, (e + P - 1) // P)) for e in en]  # contiguous renumbering: same arithmetic
+        nb = max(len(t) for t in tabs)
+        k = (rs.standard_normal((nb, P, HKV, D)) * KV_STD).astype(np.float32)
+        v = (rs.standard_normal((nb, P, HKV, D)) * KV_STD).astype(np.float32)
+        q = rs.standard_normal((sum(e - s for s, e in zip(st, en)), HQ, D)).astype(np.float32)
+        m = build_meta(tabs, en, [e - s for s, e in zip(st, en)], P)
+        t0 = time.perf_counter()
+        attend_reference(q, k, v, SCALE, m)
+        secs += time.perf_counter() - t0
+        toks += q.shape[0]
+        n += 1
+        if time.perf_counter() > t_end:
+            break
+    return {"tok_per_s": toks / (secs * L), "steps": n, "cores": cpu_threads()}
+
+
+def run_prefill(torch, bk, args, device) -> dict:
+    """Config 3 on the B200 path: every step = copy-on-write copies of the step's
+    new members, then for each of the 16 layers append_kv + attend (prefill
+    kernel), one CUDA graph per step, all steps replayed in order after one
+    warm-up pass. Reports prompt tok/s, the attention kernel's achieved
+    TFLOP/s against the measured bf16 tensor peak, and a large-batch variant
+    (the first 512-token chunk of 64 prompts in one launch)."""
+    from llm_serving_layer_b200.meta import build_meta
+
+    work = prefill_workload(args.seed + 3)
+    if work["blocks_used"] > bk.num_blocks:
+        return {"skipped": f"pool has {bk.num_blocks} blocks, config 3 needs {work['blocks_used']}"}
+    remap = {}
+    perm = np.random.RandomState(args.seed + 5).permutation(bk.num_blocks)
+    def blk(b):
+        if b not in remap:
+            remap[b] = int(perm[len(remap)])
+        return remap[b]
+    tables = {i: [blk(b) for b in t] for i, t in work["tables"].items()}
+    cows = [[(blk(a), blk(b)) for a, b in cw] for cw in work["cows"]]
+    g = torch.Generator(device=device).manual_seed(args.seed + 6)
+    TMAX = 512
+    qb = [torch.randn((TMAX, HQ, D), generator=g, device=device).half() for _ in range(L)]
+    kb = [(torch.randn((TMAX, HKV, D), generator=g, device=device) * KV_STD).half() for _ in range(L)]
+    vb = [(torch.randn((TMAX, HKV, D), generator=g, device=device) * KV_STD).half() for _ in range(L)]
+    metas, works = [], []
+    for ids, st, en in work["steps"]:
+        tabs = [tables[i][:(e + P - 1) // P] for i, e in zip(ids, en)]
+        metas.append(build_meta(tabs, en, [e - s for s, e in zip(st, en)], P, device=device))
+        works.append(prefill_step_work(ids, st, en))
+    graphs, evs = [], []
+    pool_handle = None
+    for m, cw in zip(metas, cows):
+        T = int(m.positions.shape[0])
+        for a, b in cw:  # eager first pass: warms caches, checks the kernel path
+            bk.copy_block(a, b)
+        bk.invalidate_plan()
+        bk.plan(m)
+        for layer in range(L):
+            bk.append_kv(layer, kb[layer][:T], vb[layer][:T], m)
+            bk.attend(qb[layer][:T], layer, SCALE, m)
+        assert bk.last_kernel == "prefill", bk.last_kernel
+    torch.cuda.synchronize()
+    bk.check_status()
+    for m, cw in zip(metas, cows):
+        T = int(m.positions.shape[0])
+        bk.invalidate_plan()
+        gr = torch.cuda.CUDAGraph()
+        ev = [(torch.cuda.Event(enable_timing=True, external=True),
+               torch.cuda.Event(enable_timing=True, external=True)) for _ in range(L)]
+        with torch.cuda.graph(gr, pool=pool_handle):
+            for a, b in cw:
+                bk.copy_block(a, b)
+            bk.plan(m)
+            for layer in range(L):
+                bk.append_kv(layer, kb[layer][:T], vb[layer][:T], m)
+                ev[layer][0].record()
+                bk.attend(qb[layer][:T], layer, SCALE, m)
+                ev[layer][1].record()
+        pool_handle = gr.pool()
+        graphs.append(gr)
+        evs.append(ev)
+    for gr in graphs:
+        gr.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for gr in graphs:
+        gr.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    bk.check_status()
+    ms = e0.elapsed_time(e1)
+    attn_ms = sum(a.elapsed_time(b) for ev in evs for a, b in ev)
+    flops = sum(w[0] for w in works) * L
+    peak = None
+    try:
+        peak = float(json.loads((ROOT / "MEASURED_PEAKS.json").read_text())["bf16_tflops"])
+        peak_kind = "measured"
+    except Exception:
+        peak, peak_kind = 1590.0, "fallback"
+    achieved = flops / (attn_ms / 1e3) / 1e12
+    out = {
+        "workload": ("config3: 512 prompts U[128,1024] in 32 families sharing a U[64,512]-token prefix "
+                     "(whole blocks shared through the tables, partial block copy_block'd on first write), "
+                     "steps of <= 512 prompt tokens, 16 layers append_kv + causal prefill attention, fp16"),
+        "steps": len(graphs), "computed_prompt_tokens": work["computed_tokens"],
+        "prompt_tokens": work["prompt_tokens"], "block_reuse": round(work["block_reuse"], 3),
+        "copy_on_write": work["n_cow"],
+        "tok_per_s": round(work["computed_tokens"] / (ms / 1e3), 1),
+        "prompt_tok_per_s_incl_cached": round(work["prompt_tokens"] / (ms / 1e3), 1),
+        "ms_total": round(ms, 3), "attn_ms_total": round(attn_ms, 3),
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak, "unit": "TFLOP/s",
+                     "frac": round(achieved / peak, 4), "peak_kind": peak_kind, "kernel": "prefill_kernel",
+                     "avg_launch_us": round(attn_ms * 1e3 / (len(graphs) * L), 2)},
+    }
+    del graphs
+    # large-batch variant: first 512-token chunk of 64 prompts (cached prefix s ~ U[64, 512]) in one launch
+    rs = np.random.RandomState(args.seed + 8)
+    specs = [(int(rs.randint(64, 513)), 512) for _ in range(64)]
+    tabs, o = [], 0
+    for s0, q in specs:
+        nbk = (s0 + q + P - 1) // P
+        tabs.append([int(x) for x in perm[o:o + nbk]])
+        o += nbk
+    en = [s0 + q for s0, q in specs]
+    m = build_meta(tabs, en, [q for _, q in specs], P, device=device)
+    qbig = torch.randn((sum(q for _, q in specs), HQ, D), generator=g, device=device).half()
+    bk.invalidate_plan()
+    bk.plan(m)
+    for _ in range(3):
+        bk.attend(qbig, 0, SCALE, m)
+    torch.cuda.synchronize()
+    e0.record()
+    reps = 10
+    for r in range(reps):
+        bk.attend(qbig, r % L, SCALE, m)
+    e1.record()
+    torch.cuda.synchronize()
+    bk.check_status()
+    us = e0.elapsed_time(e1) * 1e3 / reps
+    fl, _ = prefill_step_work(None, [s for s, _ in specs], en)
+    out["batched_64x512"] = {"us_per_launch": round(us, 1), "tflops": round(fl / us / 1e6, 1),
+                             "frac": round(fl / us / 1e6 / peak, 4)}
+    if args.cpu_budget > 0:
+        c = cpu_prefill_time(work, min(args.cpu_budget, 10.0))
+        out["cpu_baseline"] = {"value": round(c["tok_per_s"], 2), "unit": "tok/s", "cores": c["cores"],
+                               "kind": "port",
+                               "sample": (f"first {c['steps']} steps of the schedule, one layer each, float32 "
+                                          "numpy restatement of PagedTorchBackend.attend (prefill branch); "
+                                          "tok/s scaled to 16 layers, attention only")}
+    return out
+
+
 def run_swap(torch, bk, args, device) -> dict:
     """Config 4: 64 victims x 1024 tokens (64 blocks each, scattered), swap-out to
     pinned host and swap-in to fresh blocks, bit-exact check, alone and with a
@@ -538,6 +785,7 @@ def main() -> None:
     ap.add_argument("--e2e-steps", type=int, default=50)
     ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU oracle timing (0 = skip)")
     ap.add_argument("--no-swap", dest="swap", action="store_false")
+    ap.add_argument("--no-prefill", dest="prefill", action="store_false")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     if args.impl == "reference":
