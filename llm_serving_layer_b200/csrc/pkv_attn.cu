@@ -12,10 +12,14 @@
 //                   per-warp TMA ring (128B-swizzled, mbarrier-completed) and
 //                   does the math on tensor cores (S^T = K.Q^T, O^T += V^T.P^T,
 //                   m16n8k16, fp32 accumulate) with an fp32 online softmax.
-//                   Sequences cut by a range boundary are merged by the last
-//                   CTA to finish (atomic counter, no waiting).
-//   generic_kernel  any geometry / dtype / query length (chunked prefill,
-//                   mixed batches): one warp per (token, query head), CUDA cores.
+//                   Sequences cut by a range boundary are merged per KV head:
+//                   each consumer warp publishes its heads' partial and counts
+//                   it in (one atomic counter per (sequence, KV head)); the
+//                   warp that completes the count merges those heads (no
+//                   waiting, no CTA-wide barrier).
+//   generic_kernel  any geometry / dtype the tensor-core kernels (decode here,
+//                   prefill in pkv_prefill.cu) do not take: one warp per
+//                   (token, query head), CUDA cores.
 #include <algorithm>
 #include <array>
 #include <cstdlib>
@@ -31,8 +35,8 @@ namespace {
 constexpr int DK_D = 64;       // head_dim of the decode kernel
 constexpr int DK_P = 16;       // tokens per page of the decode kernel
 constexpr int DK_NST = 4;                  // default ring depth (pages in flight per CTA)
-constexpr int DK_MERGE_CHUNK = 16;         // split-K pieces merged per pass
-constexpr int DK_MERGE_HEADS = 64;         // query heads of the decode kernel (n_heads <= 64)
+constexpr int DK_KV_MAX = 8;               // KV heads of the decode kernel (one consumer warp each)
+constexpr int DK_WMERGE = 4;               // split-K pieces fetched per round of loads in a merge
 constexpr int DK_U = 2;                    // pages folded per online-softmax update
 #ifndef DK_TAIL_FIRST
 #define DK_TAIL_FIRST 0                    // process the range's tail piece first
@@ -45,7 +49,7 @@ constexpr int DK_MAXNREG = 168;            // 9 warps: 3 per SM sub-partition x 
 // ---------------------------------------------------------------- workspace
 struct WsLayout {
   size_t page_desc = 0;  // int4[total_pages]
-  size_t counters = 0;   // int32[n_seqs]
+  size_t counters = 0;   // int32[n_seqs][DK_KV_MAX]: split pieces counted in, per (seq, KV head)
   size_t partial_o = 0;   // float[2 * grid][n_heads][D]
   size_t partial_ml = 0;  // float2[2 * grid][n_heads]
   size_t n_tiles = 0;     // int32: prefill tiles planned (prefill layout only)
@@ -64,7 +68,7 @@ WsLayout ws_layout(int n_heads, int n_seqs, int64_t total_pages, int max_grid, i
   w.page_desc = off;
   off = align256(off + sizeof(int4) * size_t(std::max<int64_t>(total_pages, 1)));
   w.counters = off;
-  off = align256(off + sizeof(int32_t) * size_t(std::max(n_seqs, 1)));
+  off = align256(off + sizeof(int32_t) * DK_KV_MAX * size_t(std::max(n_seqs, 1)));
   w.partial_o = off;
   off = align256(off + sizeof(float) * size_t(2) * max_grid * n_heads * head_dim);
   w.partial_ml = off;
@@ -93,7 +97,7 @@ __global__ void plan_kernel(const int32_t* __restrict__ kv_indptr,
   const int lane = threadIdx.x & 31;
   if (warp >= n_seqs) return;
   const int s = warp;
-  if (lane == 0) counters[s] = 0;
+  if (lane < DK_KV_MAX) counters[size_t(s) * DK_KV_MAX + lane] = 0;
   const int64_t a = kv_indptr[s], b = kv_indptr[s + 1];
   const int lpl = last_page_len[s];
   bool bad = (a > b) || (b > total_pages) || (lpl < 1) || (lpl > block_size);
@@ -161,77 +165,80 @@ __device__ __forceinline__ void load_q_frag(const T* __restrict__ q, int row, in
   }
 }
 
-// Merge the split-K pieces cf..cl of sequence `seq` with `nthr` threads (tid
-// in [0, nthr)): per head, the running max M and normaliser W over the
-// pieces' (m, l), then every output element as sum_k w_k O_k / W. Pieces are
-// taken DK_MERGE_CHUNK at a time with a carry factor, so any number merges.
-// The participating threads synchronise with named barrier `bar` (nthr > 32)
-// or __syncwarp (one warp).
-template <typename T>
-__device__ __noinline__ void merge_pieces(const DecodeArgs& a, int seq, int64_t fa, int cf, int cl,
-                                          int64_t P, int G, int tid, int nthr, int bar,
-                                          float2* s_ml, float* sW, float* sM, float* sC,
-                                          float* s_acc) {
-  auto sync = [&]() {
-    if (nthr > 32) asm volatile("bar.sync %0, %1;" ::"r"(bar), "r"(nthr) : "memory");
-    else __syncwarp();
-  };
+// Warp h merges the split-K pieces in CTAs cf..cl of sequence `seq` for its
+// query heads h*GROUPS .. h*GROUPS + GROUPS - 1. Its own piece (CTA `own`) is
+// still in `ostage` (O/l, fp32, [GROUPS][64]) with (m, l) given per lane for
+// the head its elements belong to; every other piece's O/l and (m, l) are read
+// from the workspace, DK_WMERGE pieces per round of loads. Pieces are folded in
+// CTA order with weights l * 2^(m - M) whichever warp merges, so the result is
+// the same bits run after run. Lane `lane` owns elements [lane*PER, lane*PER + PER).
+template <typename T, int GROUPS>
+__device__ __forceinline__ void merge_warp(const DecodeArgs& a, int seq, int h, int own, int64_t fa,
+                                           int cf, int cl, int64_t P, int G, const float* ostage,
+                                           float om, float ol, int lane) {
+  constexpr int PER = GROUPS * DK_D / 32;  // 2, 4, 8 or 16 elements per lane
   const int nh = a.n_heads;
-  const int npieces = cl - cf + 1;
-  T* out = static_cast<T*>(a.out) + int64_t(seq) * nh * DK_D;
+  const int e0 = lane * PER;
+  const int j = e0 / DK_D;
   auto slot_of = [&](int cc) { return 2 * cc + ((cc == cf && fa > int64_t(cc) * P / G) ? 1 : 0); };
-  for (int k0 = 0; k0 < npieces; k0 += DK_MERGE_CHUNK) {
-    const int np = min(DK_MERGE_CHUNK, npieces - k0);
-    for (int t = tid; t < np * nh; t += nthr) {
-      const int k = t / nh, hh = t % nh;
-      s_ml[k * DK_MERGE_HEADS + hh] = __ldcg(a.partial_ml + size_t(slot_of(cf + k0 + k)) * nh + hh);
-    }
-    sync();
-    for (int hh = tid; hh < nh; hh += nthr) {
-      float M = k0 ? sM[hh] : -1e30f;
-      for (int k = 0; k < np; ++k) M = fmaxf(M, s_ml[k * DK_MERGE_HEADS + hh].x);
-      float W = 0.f;
-      for (int k = 0; k < np; ++k) {
-        float2& ml = s_ml[k * DK_MERGE_HEADS + hh];
-        const float w = ml.y * ex2(ml.x - M);
-        ml.x = w;  // from here on .x is the piece's weight
-        W += w;
-      }
-      const float carry = k0 ? ex2(sM[hh] - M) : 0.f;
-      sC[hh] = carry;
-      sW[hh] = (k0 ? sW[hh] * carry : 0.f) + W;
-      sM[hh] = M;
-    }
-    sync();
-    const bool last = k0 + np == npieces;
-    const int per = nh * DK_D / nthr;  // outputs per thread (nthr divides nh * 64)
-    for (int r0 = 0; r0 < per; r0 += 8) {
-      float acc[8];
+  float acc[PER];
 #pragma unroll
-      for (int r = 0; r < 8; ++r) {
-        const int idx = (r0 + r) * nthr + tid;
-        acc[r] = (k0 && r0 + r < per) ? s_acc[idx] * sC[idx / DK_D] : 0.f;
-      }
-      for (int k = 0; k < np; ++k) {
-        const float* po = a.partial_o + size_t(slot_of(cf + k0 + k)) * nh * DK_D;
-        float v[8];
+  for (int r = 0; r < PER; ++r) acc[r] = 0.f;
+  float M = -1e30f, W = 0.f;
+  for (int k0 = cf; k0 <= cl; k0 += DK_WMERGE) {
+    float2 ml[DK_WMERGE];
+    float v[DK_WMERGE][PER];
 #pragma unroll
-        for (int r = 0; r < 8; ++r) v[r] = (r0 + r < per) ? __ldcg(po + (r0 + r) * nthr + tid) : 0.f;
+    for (int u = 0; u < DK_WMERGE; ++u) {
+      const int cc = k0 + u;
+      ml[u] = make_float2(-1e30f, 0.f);
 #pragma unroll
-        for (int r = 0; r < 8; ++r) {
-          const int idx = (r0 + r) * nthr + tid;
-          if (r0 + r < per) acc[r] += s_ml[k * DK_MERGE_HEADS + idx / DK_D].x * v[r];
+      for (int r = 0; r < PER; ++r) v[u][r] = 0.f;
+      if (cc == own) {
+        ml[u] = make_float2(om, ol);
+#pragma unroll
+        for (int r = 0; r < PER; ++r) v[u][r] = ostage[e0 + r];
+      } else if (cc <= cl) {
+        const size_t sl = size_t(slot_of(cc));
+        ml[u] = __ldcg(a.partial_ml + sl * nh + h * GROUPS + j);
+        const float* po = a.partial_o + (sl * nh + h * GROUPS) * DK_D + e0;
+        if constexpr (PER >= 4) {
+#pragma unroll
+          for (int r = 0; r < PER; r += 4) {
+            const float4 x = __ldcg(reinterpret_cast<const float4*>(po + r));
+            v[u][r] = x.x; v[u][r + 1] = x.y; v[u][r + 2] = x.z; v[u][r + 3] = x.w;
+          }
+        } else {
+          const float2 x = __ldcg(reinterpret_cast<const float2*>(po));
+          v[u][0] = x.x; v[u][1] = x.y;
         }
       }
-#pragma unroll
-      for (int r = 0; r < 8; ++r) {
-        const int idx = (r0 + r) * nthr + tid;
-        if (r0 + r >= per) continue;
-        if (last) out[idx] = from_f<T>(acc[r] / sW[idx / DK_D]);
-        else s_acc[idx] = acc[r];
-      }
     }
-    sync();
+#pragma unroll
+    for (int u = 0; u < DK_WMERGE; ++u) {
+      if (ml[u].y <= 0.f) continue;  // not a piece of this merge (or an empty one)
+      const float Mn = fmaxf(M, ml[u].x);
+      const float cs = ex2(M - Mn), cu = ml[u].y * ex2(ml[u].x - Mn);
+#pragma unroll
+      for (int r = 0; r < PER; ++r) acc[r] = acc[r] * cs + cu * v[u][r];
+      W = W * cs + cu;
+      M = Mn;
+    }
+  }
+  const float inv = 1.f / W;
+  T* dst = static_cast<T*>(a.out) + (int64_t(seq) * nh + h * GROUPS) * DK_D + e0;
+  uint32_t pk[PER / 2];
+#pragma unroll
+  for (int r = 0; r < PER; r += 2) pk[r / 2] = MmaOp<T>::pack(acc[r] * inv, acc[r + 1] * inv);
+  if constexpr (PER == 16) {
+    reinterpret_cast<uint4*>(dst)[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+    reinterpret_cast<uint4*>(dst)[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+  } else if constexpr (PER == 8) {
+    *reinterpret_cast<uint4*>(dst) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+  } else if constexpr (PER == 4) {
+    *reinterpret_cast<uint2*>(dst) = make_uint2(pk[0], pk[1]);
+  } else {
+    *reinterpret_cast<uint32_t*>(dst) = pk[0];
   }
 }
 
@@ -324,8 +331,8 @@ __device__ __forceinline__ void attend_pages(const uint32_t (&kb)[U], const uint
 // head's 16 tokens). Consumer warp h reads its head's 2 KiB slice of each stage
 // and walks the range sequence piece by sequence piece, DK_U pages per
 // online-softmax update. A piece cut by a range boundary is written as a
-// partial (O/l, m, l) and counted in with one atomic; the CTA that completes
-// the sequence merges its pieces.
+// partial (O/l, m, l) per consumer warp and counted in with one atomic per
+// (sequence, KV head); the warp that completes a count merges those heads.
 template <typename T, int GROUPS, int NST, int MINB>
 __global__ void __maxnreg__(DK_MAXNREG) decode_kernel(const __grid_constant__ CUtensorMap tmap,
                                                       const DecodeArgs a) {
@@ -341,11 +348,6 @@ __global__ void __maxnreg__(DK_MAXNREG) decode_kernel(const __grid_constant__ CU
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + size_t(NST) * STAGE);
   uint64_t* empty = full + NST;
   float* ostage_all = reinterpret_cast<float*>(smem + size_t(NST) * STAGE + bar_bytes(2, NST));
-  // merge-warp scratch: (m, l) of a chunk of pieces per head, then their weights
-  __shared__ float2 s_ml[DK_MERGE_CHUNK * DK_MERGE_HEADS];
-  __shared__ float s_mrg_W[DK_MERGE_HEADS], s_mrg_M[DK_MERGE_HEADS], s_mrg_carry[DK_MERGE_HEADS];
-  __shared__ float s_mrg_acc[DK_MERGE_HEADS * DK_D];
-  __shared__ int s_last;
 
   const int64_t P = a.total_pages;
   const int G = gridDim.x;
@@ -570,7 +572,9 @@ __global__ void __maxnreg__(DK_MAXNREG) decode_kernel(const __grid_constant__ CU
       __syncwarp();
       continue;
     }
-    // a piece of a sequence cut by a range boundary: publish (O/l, m, l)
+    // a piece of a sequence cut by a range boundary: publish this warp's heads'
+    // (O/l, m, l), count the piece in for this KV head, and if that completes
+    // the count, merge these heads' pieces right here (no CTA-wide barrier)
     const int slot = (seq == first_seq) ? 0 : 1;
     float* po = a.partial_o + (size_t(2 * c + slot) * a.n_heads + h * GROUPS) * DK_D;
     for (int e = lane * 4; e < GROUPS * DK_D; e += 32 * 4)
@@ -580,23 +584,23 @@ __global__ void __maxnreg__(DK_MAXNREG) decode_kernel(const __grid_constant__ CU
       if (j0 < GROUPS) pml[j0] = make_float2(m0, lt0);
       if (j1 < GROUPS) pml[j1] = make_float2(m1, lt1);
     }
-    // all consumer warps count the piece in together and, if this CTA completes
-    // the sequence, merge its pieces (a CTA has at most two split pieces)
-    const int n_cons_threads = n_cons * 32;
-    asm volatile("bar.sync 1, %0;" ::"r"(n_cons_threads) : "memory");
+    __syncwarp();
     const int64_t fa = d.z, fb = d.w;
     const int cf = cta_of(fa, P, G), cl = cta_of(fb - 1, P, G);
-    if (threadIdx.x == 0) {
-      int prev;
-      asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], 1;" : "=r"(prev) : "l"(a.counters + seq) : "memory");
-      s_last = (prev == cl - cf);
+    int prev = 0;
+    int32_t* cnt = a.counters + size_t(seq) * DK_KV_MAX + h;
+    if (lane == 0) asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], 1;" : "=r"(prev) : "l"(cnt) : "memory");
+    prev = __shfl_sync(0xffffffffu, prev, 0);
+    __syncwarp();
+    if (prev == cl - cf) {
+      // this lane's head is j = lane * PER / 64; its (m, l) sit in lane j / 2 (column j & 1)
+      const int jh = (lane * GROUPS * DK_D / 32) / DK_D;
+      const float mA = __shfl_sync(0xffffffffu, m0, jh >> 1), mB = __shfl_sync(0xffffffffu, m1, jh >> 1);
+      const float lA = __shfl_sync(0xffffffffu, lt0, jh >> 1), lB = __shfl_sync(0xffffffffu, lt1, jh >> 1);
+      merge_warp<T, GROUPS>(a, seq, h, c, fa, cf, cl, P, G, ostage, (jh & 1) ? mB : mA, (jh & 1) ? lB : lA, lane);
+      if (lane == 0) *cnt = 0;
     }
-    asm volatile("bar.sync 1, %0;" ::"r"(n_cons_threads) : "memory");
-    if (s_last) {
-      merge_pieces<T>(a, seq, fa, cf, cl, P, G, threadIdx.x, n_cons_threads, 1, s_ml, s_mrg_W,
-                      s_mrg_M, s_mrg_carry, s_mrg_acc);
-      if (threadIdx.x == 0) a.counters[seq] = 0;
-    }
+    __syncwarp();
   }
 }
 
