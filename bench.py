@@ -380,7 +380,7 @@ def run_b200(args) -> None:
     line_extra = {}
     # ---- swap (config 4), rank 0 measures its own GPU's host link
     if args.swap and rank == 0:
-        line_extra["swap"] = run_swap(torch, bk, args, device)
+        line_extra["swap"] = run_swap(torch, bk, args, device, tables, ctx, qs, ks, vs)
     # ---- chunked prefill with radix sharing (config 3), rank 0
     if args.prefill and rank == 0:
         line_extra["prefill"] = run_prefill(torch, bk, args, device)
@@ -725,11 +725,14 @@ def run_prefill(torch, bk, args, device) -> dict:
     return out
 
 
-def run_swap(torch, bk, args, device) -> dict:
-    """Config 4: 64 victims x 1024 tokens (64 blocks each, scattered), swap-out to
-    pinned host and swap-in to fresh blocks, bit-exact check, alone and with a
-    concurrent batch-128 decode on the compute stream."""
+def run_swap(torch, bk, args, device, tables, ctx, qs, ks, vs) -> dict:
+    """Config 4: 64 victims x 1024 tokens (64 blocks each, scattered over blocks
+    the decode workload does not use), swap-out to pinned host and swap-in to
+    fresh blocks, bit-exact spot check; first alone, then overlapped with a
+    batch-128 decode step (16 layers, append + attend, one CUDA graph) replayed
+    back to back on the compute stream for as long as the transfers run."""
     from llm_serving_layer_b200 import B200SwapSpace
+    from llm_serving_layer_b200.meta import build_meta
 
     class Blocks:  # the block-manager view the swap space reads
         def __init__(self, ids, n):
@@ -738,39 +741,100 @@ def run_swap(torch, bk, args, device) -> dict:
     rs = np.random.RandomState(args.seed + 4)
     victims, toks = 64, 1024
     nbv = toks // P
-    perm = rs.permutation(bk.num_blocks)
-    src = [perm[i * nbv:(i + 1) * nbv].tolist() for i in range(victims)]
-    dst = [perm[(victims + i) * nbv:(victims + i + 1) * nbv].tolist() for i in range(victims)]
+    used = set(b for t in tables for b in t)
+    free = [b for b in rs.permutation(bk.num_blocks).tolist() if b not in used][: 2 * victims * nbv]
+    src = [free[i * nbv:(i + 1) * nbv] for i in range(victims)]
+    dst = [free[(victims + i) * nbv:(victims + i + 1) * nbv] for i in range(victims)]
     sw = B200SwapSpace(bk, staging_bytes=256 << 20, synchronous=False)
     per_dir = victims * sw.bytes_for(nbv)
 
-    def once():
-        torch.cuda.synchronize()
-        t0 = time.perf_counter()
-        hs = [sw.swap_out(f"v{i}", Blocks(src[i], toks)) for i in range(victims)]
-        sw.wait()
-        t1 = time.perf_counter()
-        for i, h in enumerate(hs):
-            sw.swap_in(h, Blocks(dst[i], toks))
-        sw.wait()
-        torch.cuda.synchronize()
-        t2 = time.perf_counter()
-        return hs, t1 - t0, t2 - t1
+    # the concurrent decode: first 128 sequences of the config-2 batch, one step
+    nd = 128
+    m = build_meta([t for t in tables[:nd]], ctx[:nd], [1] * nd, P, device=device)
+    bk.invalidate_plan()
+    bk.plan(m)
+    for layer in range(L):
+        bk.append_kv(layer, ks[layer][:nd], vs[layer][:nd], m)
+        bk.attend(qs[layer][:nd], layer, SCALE, m)
+    gr = torch.cuda.CUDAGraph()
+    bk.invalidate_plan()
+    with torch.cuda.graph(gr):
+        bk.plan(m)
+        for layer in range(L):
+            bk.append_kv(layer, ks[layer][:nd], vs[layer][:nd], m)
+            bk.attend(qs[layer][:nd], layer, SCALE, m)
+    for _ in range(3):
+        gr.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 200
+    e0.record()
+    for _ in range(reps):
+        gr.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    alone_ms = e0.elapsed_time(e1) / reps
 
-    hs, _, _ = once()
+    def once(with_decode):
+        torch.cuda.synchronize()
+        steps = {"out": 0, "in": 0}
+
+        def drive(kind, issue, handles_or_none):
+            n = 0
+            t0 = time.perf_counter()
+            e0.record()
+            for i in range(victims):
+                issue(i)
+                if with_decode:
+                    gr.replay()
+                    n += 1
+            if with_decode:
+                while not all(sw._lib.pkv_swapper_done(sw._sw, t) for t in handles_or_none()):
+                    for _ in range(4):  # keep the compute stream busy, the host at most 4 steps ahead
+                        gr.replay()
+                        n += 1
+                    torch.cuda.current_stream().synchronize()
+            e1.record()
+            sw.wait()
+            torch.cuda.synchronize()
+            steps[kind] = n
+            return time.perf_counter() - t0, (e0.elapsed_time(e1) / n if n else None)
+
+        hs = []
+        t_out, dec_out = drive("out", lambda i: hs.append(sw.swap_out(f"v{i}", Blocks(src[i], toks))),
+                               lambda: [h.ticket for h in hs if h.ticket])
+        tick = []
+
+        def issue_in(i):
+            sw.swap_in(hs[i], Blocks(dst[i], toks))
+            tick.append(sw._pending[-1][0] if sw._pending else 0)
+        t_in, dec_in = drive("in", issue_in, lambda: [t for t in tick if t])
+        return hs, t_out, t_in, dec_out, dec_in, steps
+
+    hs, _, _, _, _, _ = once(False)
     for h in hs:
         sw.release(h)
-    hs, t_out, t_in = once()
+    hs, t_out, t_in, _, _, _ = once(False)
     ok = True
     for i in range(0, victims, 9):  # bit-exact spot check of every 9th victim, all layers
-        a = bk._pool[:, :, src[i]]
-        b = bk._pool[:, :, dst[i]]
-        ok = ok and bool(torch.equal(a, b))
+        ok = ok and bool(torch.equal(bk._pool[:, :, src[i]], bk._pool[:, :, dst[i]]))
     for h in hs:
         sw.release(h)
+    hs, to2, ti2, dec_out, dec_in, steps = once(True)
+    for i in range(0, victims, 9):
+        ok = ok and bool(torch.equal(bk._pool[:, :, src[i]], bk._pool[:, :, dst[i]]))
+    for h in hs:
+        sw.release(h)
+    bk.check_status()
+    del gr
     return {"victims": victims, "tokens": toks, "bytes_per_direction": int(per_dir),
             "d2h_gbs": round(per_dir / t_out / 1e9, 2), "h2d_gbs": round(per_dir / t_in / 1e9, 2),
-            "bit_exact_spot_check": ok, "timing": "host wall clock around issue + wait"}
+            "bit_exact_spot_check": ok, "timing": "host wall clock around issue + wait",
+            "overlapped": {"d2h_gbs": round(per_dir / to2 / 1e9, 2), "h2d_gbs": round(per_dir / ti2 / 1e9, 2),
+                           "decode_batch": nd, "decode_ms_per_step_alone": round(alone_ms, 4),
+                           "decode_ms_per_step_during_swap_out": round(dec_out, 4) if dec_out else None,
+                           "decode_ms_per_step_during_swap_in": round(dec_in, 4) if dec_in else None,
+                           "decode_steps_during": steps}}
 
 
 def main() -> None:
