@@ -67,7 +67,9 @@ def dist_env():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled while the timed region runs."""
+    """nvidia-smi clocks / throttle reasons of the job's GPUs (comma-separated
+    UUIDs), sampled every 20 ms while the timed region runs; start() returns
+    once the first sample is in, so a short timed region is still covered."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -83,7 +85,13 @@ class ClockSampler:
             self.f = tempfile.TemporaryFile(mode="w+")
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", self.gpu_id, f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "50"], stdout=self.f, stderr=subprocess.DEVNULL)
+                 "-lms", "20"], stdout=self.f, stderr=subprocess.DEVNULL)
+            t_end = time.time() + 5.0
+            while time.time() < t_end and self.proc.poll() is None:
+                self.f.flush()
+                if os.fstat(self.f.fileno()).st_size > 0:
+                    break
+                time.sleep(0.01)
         except Exception:
             self.proc = None
 
@@ -330,12 +338,16 @@ def run_b200(args) -> None:
         gpu_id = f"GPU-{uuid}" if not str(uuid).startswith("GPU-") else str(uuid)
     except Exception:
         pass
+    if ws > 1:
+        ids = [None] * ws
+        dist.all_gather_object(ids, gpu_id)
+        gpu_id = ",".join(ids)
     clocks = ClockSampler(gpu_id)
+    if rank == 0:
+        clocks.start()
     if ws > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    clocks.start()
-    time.sleep(0.05)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for s in range(args.steps):
@@ -384,6 +396,17 @@ def run_b200(args) -> None:
     # ---- chunked prefill with radix sharing (config 3), rank 0
     if args.prefill and rank == 0:
         line_extra["prefill"] = run_prefill(torch, bk, args, device)
+    # ---- full random-init Llama-3.2-1B continuous batching (config 5), every rank a replica
+    if args.llama:
+        if ws > 1:
+            dist.barrier()
+        ll = run_llama(torch, bk, args, device, rank)
+        if ws > 1:
+            t = torch.tensor([ll["generated_tok_per_s"], ll["processed_tok_per_s"]], device=device, dtype=torch.float64)
+            dist.all_reduce(t)
+            ll["aggregate_generated_tok_per_s"] = round(float(t[0]), 1)
+            ll["aggregate_processed_tok_per_s"] = round(float(t[1]), 1)
+        line_extra["llama"] = ll
     if ws > 1:
         dist.barrier()
 
@@ -837,6 +860,148 @@ def run_swap(torch, bk, args, device, tables, ctx, qs, ks, vs) -> dict:
                            "decode_steps_during": steps}}
 
 
+def run_llama(torch, bk, args, device, rank) -> dict:
+    """Config 5: random-init Llama-3.2-1B (llm_serving_layer_b200.llama) under
+    continuous batching, through forward_varlen with this backend. Requests: a
+    final context length from config 2's lognormal (mu = ln 256 - 0.32, sigma =
+    0.8, clipped to [16, 2048], mean ~258) and a prompt of lognormal(mu = ln 32
+    - 0.32, sigma = 0.8) tokens (at most half the context); Poisson arrivals at
+    6 per step, above the completion rate, so the waiting queue never empties.
+    Up to 1024 sequences run at once; the initial ones start at a random point
+    of their lifetime with synthetic history KV. Each step decodes one token for
+    every running sequence past its prompt and prefills at most 512 prompt
+    tokens (the reference scheduler's max_prefill_tokens); a waiting request is
+    admitted when a slot is free and prefill budget is left. Greedy sampling on
+    the GPU, one host readback of the step's tokens. Wall clock per step: host
+    batch assembly (build_meta), H2D of the metadata and tokens, the 16-layer
+    forward, D2H of the tokens."""
+    from llm_serving_layer_b200.llama import LlamaConfig, RandomLlama
+    from llm_serving_layer_b200.meta import build_meta
+
+    cfg = LlamaConfig()
+    model = RandomLlama(cfg, device, seed=args.seed + 17)
+    rs = np.random.RandomState(args.seed + 18 + rank)
+    n_run, budget, lam = 1024, 512, 6.0
+
+    free = list(rs.permutation(bk.num_blocks))
+    class S:
+        __slots__ = ("blocks", "n", "prompt", "pos", "target", "last")
+    running, queue = [], []
+
+    def new_req():
+        c = int(np.clip(np.round(rs.lognormal(math.log(256) - 0.32, 0.8)), 16, 2048))
+        pl = int(np.clip(np.round(rs.lognormal(math.log(32) - 0.32, 0.8)), 4, c // 2))
+        r = S()
+        r.blocks, r.n, r.prompt, r.pos, r.target = [], 0, rs.randint(0, cfg.vocab, size=pl), 0, c
+        r.last = None
+        return r
+
+    # initial running set: somewhere inside their lifetime, history KV synthetic
+    hist_blocks = []
+    for _ in range(n_run):
+        r = new_req()
+        r.pos = len(r.prompt)
+        r.n = int(rs.randint(len(r.prompt), r.target))
+        nb = (r.n + P - 1) // P
+        r.blocks = [int(free.pop()) for _ in range(nb)]
+        hist_blocks += r.blocks
+        r.last = int(rs.randint(0, cfg.vocab))
+        running.append(r)
+    idx = torch.tensor(hist_blocks, device=device, dtype=torch.int64)
+    g = torch.Generator(device=device).manual_seed(args.seed + 19)
+    for layer in range(L):
+        for kv in range(2):
+            vals = torch.randn((idx.numel(), P, HKV, D), generator=g, device=device) * KV_STD
+            bk._pool[layer, kv].index_copy_(0, idx, vals.to(bk.dtype))
+            del vals
+    for _ in range(256):
+        queue.append(new_req())
+
+    def step():
+        pending = sum(len(r.prompt) - r.pos for r in running if r.pos < len(r.prompt))
+        while len(running) < n_run and queue and pending < budget:
+            r = queue.pop(0)
+            pending += len(r.prompt)
+            running.append(r)
+        left = budget
+        batch, qtok = [], []
+        for r in running:
+            if r.pos < len(r.prompt):
+                if left == 0:
+                    continue
+                take = min(left, len(r.prompt) - r.pos)
+                batch.append((r, take))
+                qtok.append(r.prompt[r.pos: r.pos + take])
+                left -= take
+            else:
+                batch.append((r, 1))
+                qtok.append(np.asarray([r.last]))
+        for r, q in batch:
+            need = (r.n + q + P - 1) // P - len(r.blocks)
+            for _ in range(need):
+                r.blocks.append(int(free.pop()))
+            r.n += q
+        meta = build_meta([r.blocks for r, _ in batch], [r.n for r, _ in batch], [q for _, q in batch], P,
+                          device=device)
+        toks = torch.from_numpy(np.concatenate(qtok).astype(np.int64)).pin_memory().to(device, non_blocking=True)
+        ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+        ev[0].record()
+        logits = model.forward_varlen(toks, meta, bk)
+        ev[1].record()
+        fwd_events.append(ev)
+        nxt = logits.argmax(-1).cpu().tolist()
+        gen = prompt_tok = 0
+        done = []
+        for (r, q), t in zip(batch, nxt):
+            if r.pos < len(r.prompt):
+                r.pos += q
+                prompt_tok += q
+                if r.pos < len(r.prompt):
+                    continue
+            r.last = t
+            gen += 1
+            if r.n + 1 >= r.target:
+                done.append(r)
+        for r in done:
+            running.remove(r)
+            free.extend(r.blocks)
+        for _ in range(rs.poisson(lam)):
+            queue.append(new_req())
+        return gen, prompt_tok, len(batch), int(meta.positions.shape[0])
+
+    fwd_events = []
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    bk.check_status()
+    fwd_events.clear()
+    steps = max(20, min(args.llama_steps, 1000))
+    gens = prompts = seqs = toks = 0
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        a_, b_, c_, d_ = step()
+        gens += a_
+        prompts += b_
+        seqs += c_
+        toks += d_
+    torch.cuda.synchronize()
+    dt = time.perf_counter() - t0
+    bk.check_status()
+    fwd_ms = sum(a.elapsed_time(b) for a, b in fwd_events) / len(fwd_events)
+    del model
+    torch.cuda.empty_cache()
+    return {"workload": ("config5: random-init Llama-3.2-1B (hidden 2048, 16 layers, 32/8 heads, d 64, FFN 8192, "
+                         "vocab 128256, RoPE theta 500000, fp16), continuous batching of up to 1024 sequences, "
+                         "final context lognormal mean ~258 cap 2048, prompts lognormal mean ~32, Poisson "
+                         "arrivals 6/step, <= 512 prefill tokens per step, greedy"),
+            "steps": steps, "generated_tok_per_s": round(gens / dt, 1),
+            "processed_tok_per_s": round(toks / dt, 1), "prompt_tok_per_s": round(prompts / dt, 1),
+            "ms_per_step": round(dt * 1e3 / steps, 3), "forward_device_ms_per_step": round(fwd_ms, 3),
+            "mean_batch_seqs": round(seqs / steps, 1),
+            "mean_batch_tokens": round(toks / steps, 1),
+            "timing": "host wall clock around the steps (host scheduling, batch assembly, H2D, forward, D2H)"}
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -850,6 +1015,8 @@ def main() -> None:
     ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU oracle timing (0 = skip)")
     ap.add_argument("--no-swap", dest="swap", action="store_false")
     ap.add_argument("--no-prefill", dest="prefill", action="store_false")
+    ap.add_argument("--no-llama", dest="llama", action="store_false")
+    ap.add_argument("--llama-steps", type=int, default=100)
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     if args.impl == "reference":
