@@ -623,18 +623,53 @@ def run_prefill(torch, bk, args, device) -> dict:
     (the first 512-token chunk of 64 prompts in one launch)."""
     from llm_serving_layer_b200.meta import build_meta
 
+    try:
+        peak = float(json.loads((ROOT / "MEASURED_PEAKS.json").read_text())["bf16_tflops"])
+        peak_kind = "measured"
+    except Exception:
+        peak, peak_kind = 1590.0, "fallback"
     work = prefill_workload(args.seed + 3)
-    if work["blocks_used"] > bk.num_blocks:
-        return {"skipped": f"pool has {bk.num_blocks} blocks, config 3 needs {work['blocks_used']}"}
-    remap = {}
     perm = np.random.RandomState(args.seed + 5).permutation(bk.num_blocks)
+    g = torch.Generator(device=device).manual_seed(args.seed + 6)
+    # large-batch variant (run first, so its launches are the first prefill launches of the
+    # process): the first 512-token chunk of 64 prompts (cached prefix s ~ U[64, 512]) in one launch
+    rs = np.random.RandomState(args.seed + 8)
+    specs = [(int(rs.randint(64, 513)), 512) for _ in range(64)]
+    tabs, o = [], 0
+    for s0, q in specs:
+        nbk = (s0 + q + P - 1) // P
+        tabs.append([int(x) for x in perm[o:o + nbk]])
+        o += nbk
+    en = [s0 + q for s0, q in specs]
+    m = build_meta(tabs, en, [q for _, q in specs], P, device=device)
+    qbig = torch.randn((sum(q for _, q in specs), HQ, D), generator=g, device=device).half()
+    bk.invalidate_plan()
+    bk.plan(m)
+    for _ in range(3):
+        bk.attend(qbig, 0, SCALE, m)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    reps = 10
+    for r in range(reps):
+        bk.attend(qbig, r % L, SCALE, m)
+    e1.record()
+    torch.cuda.synchronize()
+    bk.check_status()
+    us = e0.elapsed_time(e1) * 1e3 / reps
+    fl, _ = prefill_step_work(None, [s for s, _ in specs], en)
+    batched = {"us_per_launch": round(us, 1), "tflops": round(fl / us / 1e6, 1), "frac": round(fl / us / 1e6 / peak, 4)}
+    del qbig
+    if work["blocks_used"] > bk.num_blocks:
+        return {"skipped": f"pool has {bk.num_blocks} blocks, config 3 needs {work['blocks_used']}",
+                "batched_64x512": batched}
+    remap = {}
     def blk(b):
         if b not in remap:
             remap[b] = int(perm[len(remap)])
         return remap[b]
     tables = {i: [blk(b) for b in t] for i, t in work["tables"].items()}
     cows = [[(blk(a), blk(b)) for a, b in cw] for cw in work["cows"]]
-    g = torch.Generator(device=device).manual_seed(args.seed + 6)
     TMAX = 512
     qb = [torch.randn((TMAX, HQ, D), generator=g, device=device).half() for _ in range(L)]
     kb = [(torch.randn((TMAX, HKV, D), generator=g, device=device) * KV_STD).half() for _ in range(L)]
@@ -689,12 +724,6 @@ def run_prefill(torch, bk, args, device) -> dict:
     ms = e0.elapsed_time(e1)
     attn_ms = sum(a.elapsed_time(b) for ev in evs for a, b in ev)
     flops = sum(w[0] for w in works) * L
-    peak = None
-    try:
-        peak = float(json.loads((ROOT / "MEASURED_PEAKS.json").read_text())["bf16_tflops"])
-        peak_kind = "measured"
-    except Exception:
-        peak, peak_kind = 1590.0, "fallback"
     achieved = flops / (attn_ms / 1e3) / 1e12
     out = {
         "workload": ("config3: 512 prompts U[128,1024] in 32 families sharing a U[64,512]-token prefix "
@@ -709,35 +738,9 @@ def run_prefill(torch, bk, args, device) -> dict:
         "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak, "unit": "TFLOP/s",
                      "frac": round(achieved / peak, 4), "peak_kind": peak_kind, "kernel": "prefill_kernel",
                      "avg_launch_us": round(attn_ms * 1e3 / (len(graphs) * L), 2)},
+        "batched_64x512": batched,
     }
     del graphs
-    # large-batch variant: first 512-token chunk of 64 prompts (cached prefix s ~ U[64, 512]) in one launch
-    rs = np.random.RandomState(args.seed + 8)
-    specs = [(int(rs.randint(64, 513)), 512) for _ in range(64)]
-    tabs, o = [], 0
-    for s0, q in specs:
-        nbk = (s0 + q + P - 1) // P
-        tabs.append([int(x) for x in perm[o:o + nbk]])
-        o += nbk
-    en = [s0 + q for s0, q in specs]
-    m = build_meta(tabs, en, [q for _, q in specs], P, device=device)
-    qbig = torch.randn((sum(q for _, q in specs), HQ, D), generator=g, device=device).half()
-    bk.invalidate_plan()
-    bk.plan(m)
-    for _ in range(3):
-        bk.attend(qbig, 0, SCALE, m)
-    torch.cuda.synchronize()
-    e0.record()
-    reps = 10
-    for r in range(reps):
-        bk.attend(qbig, r % L, SCALE, m)
-    e1.record()
-    torch.cuda.synchronize()
-    bk.check_status()
-    us = e0.elapsed_time(e1) * 1e3 / reps
-    fl, _ = prefill_step_work(None, [s for s, _ in specs], en)
-    out["batched_64x512"] = {"us_per_launch": round(us, 1), "tflops": round(fl / us / 1e6, 1),
-                             "frac": round(fl / us / 1e6 / peak, 4)}
     if args.cpu_budget > 0:
         c = cpu_prefill_time(work, min(args.cpu_budget, 10.0))
         out["cpu_baseline"] = {"value": round(c["tok_per_s"], 2), "unit": "tok/s", "cores": c["cores"],
