@@ -751,11 +751,12 @@ struct TmapEntry {
   int device;
   void* base;
   int64_t num_blocks;
-  int num_layers, block_size, n_kv_heads, head_dim, dtype;
+  int num_layers, block_size, n_kv_heads, head_dim, dtype, box_heads;
   CUtensorMap map;
 };
 
-int get_tmap(const pkv_pool& p, CUtensorMap* out) {
+// box_heads: KV heads per box (the pool's n_kv_heads for whole pages, 1 for one head's slice)
+int get_tmap(const pkv_pool& p, CUtensorMap* out, int box_heads) {
   static std::mutex mu;
   static std::vector<TmapEntry> cache;
   int dev = 0;
@@ -764,7 +765,8 @@ int get_tmap(const pkv_pool& p, CUtensorMap* out) {
   for (const auto& e : cache) {
     if (e.device == dev && e.base == p.base && e.num_blocks == p.num_blocks &&
         e.num_layers == p.num_layers && e.block_size == p.block_size &&
-        e.n_kv_heads == p.n_kv_heads && e.head_dim == p.head_dim && e.dtype == p.dtype) {
+        e.n_kv_heads == p.n_kv_heads && e.head_dim == p.head_dim && e.dtype == p.dtype &&
+        e.box_heads == box_heads) {
       *out = e.map;
       return PKV_OK;
     }
@@ -779,16 +781,16 @@ int get_tmap(const pkv_pool& p, CUtensorMap* out) {
     encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
   }
   const int es = elem_size(p.dtype);
-  TmapEntry e{dev, p.base, p.num_blocks, p.num_layers, p.block_size, p.n_kv_heads, p.head_dim, p.dtype, {}};
+  TmapEntry e{dev, p.base, p.num_blocks, p.num_layers, p.block_size, p.n_kv_heads, p.head_dim, p.dtype,
+              box_heads, {}};
   // Permuted view of the pool: dims (D, token slot, KV head, layer*2+kv) with
-  // strides (elem, row, head_dim*elem, slab). One box = one whole page of one
-  // layer's K or V, landing in shared memory as [head][token][D].
+  // strides (elem, row, head_dim*elem, slab). One box = one page of one layer's
+  // K or V for box_heads heads, landing in shared memory as [head][token][D].
   const cuuint64_t dims[4] = {cuuint64_t(p.head_dim), cuuint64_t(p.num_blocks) * p.block_size,
                               cuuint64_t(p.n_kv_heads), cuuint64_t(2) * p.num_layers};
   const cuuint64_t strides[3] = {cuuint64_t(row_bytes(p)), cuuint64_t(p.head_dim) * es,
                                  cuuint64_t(slab_bytes(p))};
-  const cuuint32_t box[4] = {cuuint32_t(p.head_dim), cuuint32_t(p.block_size),
-                             cuuint32_t(p.n_kv_heads), 1u};
+  const cuuint32_t box[4] = {cuuint32_t(p.head_dim), cuuint32_t(p.block_size), cuuint32_t(box_heads), 1u};
   const cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
   const CUtensorMapDataType dt =
       p.dtype == PKV_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
@@ -924,7 +926,8 @@ WsLayout step_layout(const pkv_pool* pool, int n_heads, int n_seqs, int64_t tota
 
 }  // namespace
 
-int pool_tmap(const pkv_pool& p, CUtensorMap* out) { return get_tmap(p, out); }
+int pool_tmap(const pkv_pool& p, CUtensorMap* out) { return get_tmap(p, out, p.n_kv_heads); }
+int pool_tmap_head(const pkv_pool& p, CUtensorMap* out) { return get_tmap(p, out, 1); }
 
 }  // namespace pkv
 
@@ -989,7 +992,7 @@ extern "C" int pkv_attend_planned(const pkv_pool* pool, int32_t layer, int32_t n
     if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(out)) & 15)
       return fail(PKV_ERR_ARG, "q and out must be 16-byte aligned");
     CUtensorMap tm;
-    if (int rc = get_tmap(p, &tm)) return rc;
+    if (int rc = get_tmap(p, &tm, p.n_kv_heads)) return rc;
     char* ws = static_cast<char*>(workspace);
     DecodeArgs a;
     a.q = q;
@@ -1181,7 +1184,7 @@ extern "C" int pkv_attend_decode_noalloc(const pkv_pool* pool, int32_t layer, in
       batch->dev_status);
   PKV_CUDA_RET(cudaGetLastError());
   CUtensorMap tm;
-  if (int rc = get_tmap(p, &tm)) return rc;
+  if (int rc = get_tmap(p, &tm, p.n_kv_heads)) return rc;
   DecodeArgs a;
   a.q = q;
   a.out = out;

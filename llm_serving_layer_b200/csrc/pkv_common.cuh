@@ -52,6 +52,8 @@ int num_sms();  // SM count of the current device (cached per device)
 // layer*2+kv; one box = one whole [8 heads][16 tok][64] page of one layer's K
 // or V), cached per (device, pool). pkv_attn.cu.
 int pool_tmap(const pkv_pool& p, CUtensorMap* out);
+// The same view with one KV head per box ([16 tok][64], 2 KiB for fp16).
+int pool_tmap_head(const pkv_pool& p, CUtensorMap* out);
 
 // Chunked-prefill / mixed-batch tensor-core attention (pkv_prefill.cu).
 bool prefill_supported(const pkv_pool& p, int n_heads);
@@ -62,6 +64,11 @@ int prefill_plan(const pkv_pool& p, int n_heads, const pkv_batch& b, int2* tiles
 int prefill_attend(const pkv_pool& p, int layer, int n_heads, const void* q, void* out, float scale,
                    const pkv_batch& b, const int2* tiles, const int32_t* n_tiles, int64_t tiles_cap,
                    cudaStream_t s);
+// The tcgen05 / TMEM variant (pkv_prefill_tc.cu); prefill_attend dispatches to it.
+int prefill_tc_tile_tokens(int n_heads, int n_kv_heads);
+int prefill_tc_attend(const pkv_pool& p, int layer, int n_heads, const void* q, void* out, float scale,
+                      const pkv_batch& b, const int2* tiles, const int32_t* n_tiles, int64_t tiles_cap,
+                      cudaStream_t s);
 
 // ---------------------------------------------------------------- device side
 __device__ __forceinline__ void flag(int32_t* st, int32_t bits) {

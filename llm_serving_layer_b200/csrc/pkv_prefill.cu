@@ -18,6 +18,7 @@
 // mask triu(diag = kv_len - q_len + 1) (paged_torch.py:470-476), and the
 // unwritten tail of a sequence's last page never reaches the output.
 #include <algorithm>
+#include <cstdlib>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -478,7 +479,18 @@ bool prefill_supported(const pkv_pool& p, int n_heads) {
   return gq == 1 || gq == 2 || gq == 4 || gq == 8;
 }
 
-int prefill_tile_tokens(int n_heads, int n_kv_heads) { return 2 * (PF_ROWS / (n_heads / n_kv_heads)); }
+// The tcgen05 kernel (pkv_prefill_tc.cu) is the default; PKV_PREFILL_TC=0 selects
+// this file's mma.sync kernel (for comparisons). Read at every plan and every
+// launch, so it must not change between a step's plan and its attends.
+bool prefill_use_tc() {
+  const char* e = getenv("PKV_PREFILL_TC");
+  return !(e && e[0] == '0');
+}
+
+int prefill_tile_tokens(int n_heads, int n_kv_heads) {
+  if (prefill_use_tc()) return prefill_tc_tile_tokens(n_heads, n_kv_heads);
+  return 2 * (PF_ROWS / (n_heads / n_kv_heads));
+}
 
 int64_t prefill_tiles_cap(int n_seqs, int64_t total_pages) {
   // tiles <= n_tokens / QT + n_seqs with QT >= 8 and n_tokens <= 16 * total_pages
@@ -499,6 +511,7 @@ int prefill_plan(const pkv_pool& p, int n_heads, const pkv_batch& b, int2* tiles
 int prefill_attend(const pkv_pool& p, int layer, int n_heads, const void* q, void* out, float scale,
                    const pkv_batch& b, const int2* tiles, const int32_t* n_tiles, int64_t tiles_cap,
                    cudaStream_t s) {
+  if (prefill_use_tc()) return prefill_tc_attend(p, layer, n_heads, q, out, scale, b, tiles, n_tiles, tiles_cap, s);
   if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(out)) & 15)
     return fail(PKV_ERR_ARG, "q and out must be 16-byte aligned");
   CUtensorMap tm;

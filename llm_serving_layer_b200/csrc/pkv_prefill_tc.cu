@@ -1,0 +1,511 @@
+// pkv_prefill_tc.cu — chunked-prefill / mixed-batch attention on the
+// 5th-generation tensor cores: tcgen05 MMAs with their accumulators in tensor
+// memory (TMEM), operands staged in shared memory by TMA.
+//
+// One CTA = one tile of query rows of one sequence for ONE KV head: 128 rows =
+// TPT = 128 / G tokens x the G query heads that share the KV head (row
+// r = head * TPT + token). Warp roles:
+//   warp 0      TMA producer: one 2 KiB box per page per K and V (that head's
+//               [16 tok][64] slice), 4 pages = one 64-key block per stage,
+//               4 stages; pages past the tile's last visible key read the
+//               zero fill of a negative coordinate.
+//   warp 1      allocates 256 TMEM columns; one thread issues the MMAs:
+//                 S_j  [128 x 64]  = Q [128 x 64] . K_j^T      (SS: A and B
+//                                    from shared memory, K-major, 128B swizzle)
+//                 O   [128 x 64] += P_j [128 x 64] . V_j        (TS: A = P from
+//                                    TMEM, B = V MN-major from shared memory)
+//               S is double-buffered in TMEM (columns 0-63 / 64-127), P is
+//               written over the first 32 columns of its S buffer as packed
+//               16-bit pairs, O lives in columns 128-191. Completion is
+//               signalled with tcgen05.commit to mbarriers.
+//   warps 2-5   softmax, one thread per row (warp w reads TMEM lanes
+//               32*(w%4) .. +31): tcgen05.ld of the row's 64 scores, scale,
+//               bottom-right causal mask key <= kv_len - q_len + j (which also
+//               masks the unwritten tail of the last page), running max with a
+//               lazy O rescale (only when the max grows by more than 2^8),
+//               exp2, P to TMEM with tcgen05.st; epilogue O / l -> global.
+// The unwritten tail rows of the sequence's last page are zeroed in the V
+// stage before its P.V MMA, so stale (even NaN) data there meets P = 0 as 0.
+//
+// Semantics are PagedTorchBackend.attend's (serving/backends/paged_torch.py:
+// 400-485): GQA head h reads KV head h // G, pages in listed order, mask
+// triu(diag = kv_len - q_len + 1).
+#include <mutex>
+#include <string>
+#include <type_traits>
+#include <vector>
+
+#include "pkv_common.cuh"
+
+namespace pkv {
+namespace {
+
+constexpr int TC_D = 64;                      // head_dim
+constexpr int TC_P = 16;                      // tokens per page
+constexpr int TC_ROWS = 128;                  // query rows per CTA (UMMA M)
+constexpr int TC_KB = 64;                     // keys per block (UMMA N of S)
+constexpr int TC_PPB = TC_KB / TC_P;          // pages per block
+constexpr int TC_NST = 4;                     // K/V stages
+constexpr int TC_PAGE = TC_P * TC_D * 2;      // 2 KiB: one head's slice of a page
+constexpr int TC_KTILE = TC_KB * TC_D * 2;    // 8 KiB
+constexpr int TC_STAGE = 2 * TC_KTILE;        // K + V
+constexpr int TC_QTILE = TC_ROWS * TC_D * 2;  // 16 KiB
+constexpr int TC_TMEM_COLS = 256;
+constexpr int TC_THREADS = 192;
+constexpr float TC_RESCALE = 8.f;             // rescale O when the max grows by > 2^8
+
+struct TcArgs {
+  const void* q;
+  void* out;
+  const int32_t* cu_q;
+  const int32_t* kv_lens;
+  const int32_t* kv_indptr;
+  const int32_t* kv_indices;
+  const int32_t* last_page_len;
+  const int2* tiles;
+  const int32_t* n_tiles;
+  int32_t* st;
+  int64_t num_blocks;
+  int64_t total_pages;
+  int n_seqs, n_tokens, n_heads, n_kv, layer;
+  float scale_log2;
+};
+
+// ---------------------------------------------------------------- tcgen05 helpers
+// Shared-memory matrix descriptor, 128B swizzle: start address, leading byte
+// offset 16 B (unused by swizzled K-major; one 64-element atom in MN), stride
+// byte offset 1024 B between 8-row groups, descriptor version 1.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  return uint64_t((saddr >> 4) & 0x3FFFu) | (uint64_t(1) << 16) | (uint64_t(1024 >> 4) << 32) |
+         (uint64_t(1) << 46) | (uint64_t(2) << 61);
+}
+// Instruction descriptor of kind::f16: fp32 accumulate, A/B element format
+// (0 = f16, 1 = bf16, always equal), A K-major, B K- or MN-major, N, M = 128.
+__host__ __device__ constexpr uint32_t idesc_f16(int fmt, int b_mn_major, int n) {
+  return (1u << 4) | (uint32_t(fmt) << 7) | (uint32_t(fmt) << 10) | (uint32_t(b_mn_major) << 16) |
+         (uint32_t(n >> 3) << 17) | (uint32_t(TC_ROWS >> 4) << 24);
+}
+__device__ __forceinline__ void umma_ss(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+__device__ __forceinline__ void umma_ts(uint32_t d, uint32_t a_tmem, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+// arrive on `bar` once every tcgen05 operation this thread issued so far completed
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+#define PKV_R8(i) "=r"(r[i]), "=r"(r[i + 1]), "=r"(r[i + 2]), "=r"(r[i + 3]), "=r"(r[i + 4]), "=r"(r[i + 5]), "=r"(r[i + 6]), "=r"(r[i + 7])
+#define PKV_W8(i) "r"(r[i]), "r"(r[i + 1]), "r"(r[i + 2]), "r"(r[i + 3]), "r"(r[i + 4]), "r"(r[i + 5]), "r"(r[i + 6]), "r"(r[i + 7])
+
+// 32 consecutive 32-bit TMEM columns of this thread's lane; waits for the load
+// inside the same asm statement, so the registers are valid when it returns.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : PKV_R8(0), PKV_R8(8), PKV_R8(16), PKV_R8(24)
+      : "r"(taddr)
+      : "memory");
+}
+// 32 consecutive 32-bit TMEM columns of this thread's lane <- r; waits for the store.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};\n\t"
+      "tcgen05.wait::st.sync.aligned;" ::"r"(taddr),
+      PKV_W8(0), PKV_W8(8), PKV_W8(16), PKV_W8(24)
+      : "memory");
+}
+#undef PKV_R8
+#undef PKV_W8
+
+__device__ __forceinline__ int tc_tile_pages(int64_t kv, int ql, int j0, int qt) {
+  if (kv < ql || ql < 1) return 0;
+  const int jl = min(j0 + qt, ql) - 1;
+  return int((kv - ql + jl) / TC_P + 1);
+}
+
+template <typename T, int G>
+__global__ void __launch_bounds__(TC_THREADS, 2) prefill_tc_kernel(const __grid_constant__ CUtensorMap tmap,
+                                                                   const TcArgs a) {
+  constexpr int TPT = TC_ROWS / G;  // tokens per tile
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char* qs = smem;                    // [128 rows][128 B], 128B swizzle
+  unsigned char* stages = smem + TC_QTILE;     // TC_NST x {K [64][128 B], V [64][128 B]}
+  uint64_t* full = reinterpret_cast<uint64_t*>(stages + size_t(TC_NST) * TC_STAGE);
+  uint64_t* empty = full + TC_NST;             // P.V of the stage's block completed
+  uint64_t* s_full = empty + TC_NST;           // [2] S block in TMEM
+  uint64_t* p_full = s_full + 2;               // [2] P in TMEM (and O rescaled), 128 arrivals
+  uint64_t* o_done = p_full + 2;               // one phase per P.V block
+  uint64_t* q_ready = o_done + 1;              // Q tile in shared memory, 128 arrivals
+  uint64_t* drain = q_ready + 1;               // every MMA of the CTA completed
+  __shared__ uint32_t s_tmem;
+  __shared__ int s_bad;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tile_idx = int(blockIdx.x) / a.n_kv, h = int(blockIdx.x) % a.n_kv;
+  if (tile_idx >= *a.n_tiles) return;
+  const int2 tile = a.tiles[tile_idx];
+  const int s = tile.x, j0 = tile.y;
+  bool bad = s < 0 || s >= a.n_seqs;
+  int q0 = 0, ql = 0, lpl = 0;
+  int64_t pa = 0, pb = 0;
+  if (!bad) {
+    q0 = a.cu_q[s];
+    ql = a.cu_q[s + 1] - q0;
+    pa = a.kv_indptr[s];
+    pb = a.kv_indptr[s + 1];
+    lpl = a.last_page_len[s];
+  }
+  const int64_t npages64 = pb - pa;
+  const int64_t kv64 = (npages64 - 1) * TC_P + lpl;
+  bad = bad || npages64 < 1 || pa < 0 || pb > a.total_pages || lpl < 1 || lpl > TC_P || ql < 1 ||
+        j0 < 0 || j0 >= ql || kv64 < ql || kv64 >= 0x7fffffff || q0 < 0 || q0 + ql > a.n_tokens;
+  if (!bad && a.kv_lens && a.kv_lens[s] != kv64) bad = true;
+  const int kv = bad ? 0 : int(kv64);
+  const int npages = bad ? 0 : int(npages64);
+  const int n_pg = bad ? 0 : tc_tile_pages(kv, ql, j0, TPT);  // pages with keys visible to the tile
+  const int nblk = (n_pg + TC_PPB - 1) / TC_PPB;
+  if (threadIdx.x == 0) s_bad = bad ? 1 : 0;
+  __syncthreads();
+  for (int i = threadIdx.x; i < n_pg; i += blockDim.x) {
+    const int id = a.kv_indices[pa + i];
+    if (id < 0 || id >= a.num_blocks) s_bad = 2;
+  }
+  if (threadIdx.x == 0) {
+    prefetch_tmap(&tmap);
+    for (int i = 0; i < TC_NST; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 128);
+    }
+    mbar_init(o_done, 1);
+    mbar_init(q_ready, 128);
+    mbar_init(drain, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  T* out = static_cast<T*>(a.out);
+  // row r of the tile: query head h * G + r / TPT, chunk-relative token j0 + r % TPT
+  auto out_row = [&](int r) -> T* {
+    const int j = j0 + r % TPT;
+    return j < ql ? out + ((int64_t(q0) + j) * a.n_heads + h * G + r / TPT) * TC_D : nullptr;
+  };
+  if (s_bad) {  // before any TMA or TMEM use
+    if (threadIdx.x == 0) flag(a.st, s_bad == 1 ? PKV_DEV_META_BAD : PKV_DEV_SLOT_OOB);
+    if (s_bad == 2 && warp >= 2) {
+      if (T* o = out_row((warp & 3) * 32 + lane))
+        for (int c = 0; c < 8; ++c) reinterpret_cast<uint4*>(o)[c] = make_uint4(0u, 0u, 0u, 0u);
+    }
+    return;
+  }
+
+  // ---- tensor memory: 256 columns (S0, S1, O), freed on every path below
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
+                 "r"(TC_TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = s_tmem;
+  const uint32_t tO = tbase + 128;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      const int kvc = 2 * a.layer;
+      int issued = 0;
+      bool dead = false;
+      for (int j = 0; j < nblk; ++j) {
+        const int st = j % TC_NST;
+        if (j >= TC_NST && !mbar_wait_bounded_sleepy(&empty[st], ((j / TC_NST) - 1) & 1, a.st, 64)) {
+          dead = true;
+          break;
+        }
+        unsigned char* kd = stages + size_t(st) * TC_STAGE;
+        mbar_arrive_expect_tx(&full[st], TC_STAGE);
+#pragma unroll
+        for (int u = 0; u < TC_PPB; ++u) {
+          const int pg = j * TC_PPB + u;
+          // a page past the tile's visible keys reads the zero fill of a negative coordinate
+          const int row = pg < n_pg ? a.kv_indices[pa + pg] * TC_P : -TC_P;
+          tma_load_4d(kd + u * TC_PAGE, &tmap, &full[st], 0, row, h, kvc);
+          tma_load_4d(kd + TC_KTILE + u * TC_PAGE, &tmap, &full[st], 0, row, h, kvc + 1);
+        }
+        issued = j + 1;
+      }
+      // let this CTA's own copies land before its shared memory can be released
+      if (dead)
+        for (int i = max(0, issued - TC_NST); i < issued; ++i)
+          mbar_wait_bounded(&full[i % TC_NST], (i / TC_NST) & 1, nullptr);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    constexpr int fmt = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
+    constexpr uint32_t idS = idesc_f16(fmt, 0, TC_KB);
+    constexpr uint32_t idPV = idesc_f16(fmt, 1, TC_D);
+    const uint32_t q_addr = smem_u32(qs);
+    bool dead = !mbar_wait_bounded(q_ready, 0, a.st);
+    dead = __any_sync(0xffffffffu, dead);
+    const int lp_blk = (npages - 1) / TC_PPB;  // block holding the sequence's last page
+    for (int j = 0; j <= nblk && !dead; ++j) {
+      if (j < nblk) {
+        const int st = j % TC_NST;
+        if (!mbar_wait_bounded(&full[st], (j / TC_NST) & 1, a.st)) dead = true;
+        dead = __any_sync(0xffffffffu, dead);
+        if (dead) break;
+        if (j == lp_blk && lpl < TC_P && npages - 1 < n_pg) {
+          // rows lpl..15 of the last page's V slice were never written: zero them
+          uint4* vt = reinterpret_cast<uint4*>(stages + size_t(st) * TC_STAGE + TC_KTILE +
+                                               (npages - 1 - j * TC_PPB) * TC_PAGE);
+          for (int r = lpl * 8 + lane; r < TC_P * 8; r += 32) vt[r] = make_uint4(0u, 0u, 0u, 0u);
+          fence_proxy_async_smem();
+          __syncwarp();
+        }
+        if (lane == 0) {
+          tc_fence_after();
+          const uint32_t kaddr = smem_u32(stages + size_t(st) * TC_STAGE);
+          const uint32_t dS = tbase + (j & 1) * TC_KB;
+#pragma unroll
+          for (int k = 0; k < TC_D / 16; ++k)
+            umma_ss(dS, sw128_desc(q_addr + 32 * k), sw128_desc(kaddr + 32 * k), idS, k > 0);
+          umma_commit(&s_full[j & 1]);
+        }
+        __syncwarp();
+      }
+      if (j >= 1) {
+        const int jp = j - 1, stp = jp % TC_NST;
+        if (!mbar_wait_bounded(&p_full[jp & 1], (jp >> 1) & 1, a.st)) dead = true;
+        dead = __any_sync(0xffffffffu, dead);
+        if (dead) break;
+        if (lane == 0) {
+          tc_fence_after();
+          const uint32_t vaddr = smem_u32(stages + size_t(stp) * TC_STAGE + TC_KTILE);
+          const uint32_t aP = tbase + (jp & 1) * TC_KB;
+#pragma unroll
+          for (int k = 0; k < TC_KB / 16; ++k)
+            umma_ts(tO, aP + 8 * k, sw128_desc(vaddr + 16 * 128 * k), idPV, (jp > 0 || k > 0) ? 1u : 0u);
+          umma_commit(o_done);
+          umma_commit(&empty[stp]);
+        }
+        __syncwarp();
+      }
+    }
+    // every MMA issued above has completed before TMEM is freed
+    if (lane == 0) {
+      umma_commit(drain);
+      mbar_wait_bounded(drain, 0, a.st);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ softmax warps
+    const int q4 = warp & 3;  // TMEM lane quarter this warp may access
+    const int r = q4 * 32 + lane;
+    const int jq = j0 + r % TPT;
+    const bool valid = jq < ql;
+    const int lim = valid ? kv - ql + jq : -1;  // last visible key of this row
+    {
+      const T* qg = static_cast<const T*>(a.q);
+      const uint4* src = reinterpret_cast<const uint4*>(qg + ((int64_t(q0) + jq) * a.n_heads + h * G + r / TPT) * TC_D);
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const uint4 v = valid ? __ldg(src + c) : make_uint4(0u, 0u, 0u, 0u);
+        *reinterpret_cast<uint4*>(qs + r * 128 + ((c ^ (r & 7)) << 4)) = v;
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(q_ready);
+    }
+    const uint32_t lane_off = uint32_t(q4 * 32) << 16;
+    const float sl2 = a.scale_log2;
+    float m = -INFINITY, l = 0.f;
+    bool dead = false;
+    for (int j = 0; j < nblk; ++j) {
+      const int b = j & 1;
+      if (!mbar_wait_bounded(&s_full[b], (j >> 1) & 1, a.st)) dead = true;
+      // O may be rescaled (and P overwritten next round) only after the previous P.V
+      if (j >= 1 && !dead && !mbar_wait_bounded(o_done, (j - 1) & 1, a.st)) dead = true;
+      dead = __any_sync(0xffffffffu, dead);
+      if (dead) break;
+      tc_fence_after();
+      uint32_t sr[2][32];
+      tmem_ld32(tbase + lane_off + b * TC_KB, sr[0]);
+      tmem_ld32(tbase + lane_off + b * TC_KB + 32, sr[1]);
+      const int kb0 = j * TC_KB;
+      const bool tail = kb0 + TC_KB - 1 > lim;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf)
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          float x = __uint_as_float(sr[hf][i]) * sl2;
+          if (tail && kb0 + hf * 32 + i > lim) x = -INFINITY;
+          sr[hf][i] = __float_as_uint(x);
+          mx = fmaxf(mx, x);
+        }
+      const float mn = fmaxf(m, mx);
+      float m_new = m;
+      if (mn != -INFINITY && (m == -INFINITY || mn > m + TC_RESCALE)) m_new = mn;
+      const bool resc = (m_new != m) && (m != -INFINITY);  // earlier blocks already added to O
+      const float alpha = resc ? ex2(m - m_new) : 1.f;
+      l *= alpha;
+      m = m_new;
+      if (__any_sync(0xffffffffu, resc)) {
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          uint32_t o[32];
+          tmem_ld32(tO + lane_off + hf * 32, o);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st32(tO + lane_off + hf * 32, o);
+        }
+      }
+      const float mu = m == -INFINITY ? 0.f : m;
+      float ls = 0.f;
+      uint32_t pk[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const int e = 2 * i;
+        const float p0 = ex2(__uint_as_float(sr[e >> 5][e & 31]) - mu);
+        const float p1 = ex2(__uint_as_float(sr[(e + 1) >> 5][(e + 1) & 31]) - mu);
+        ls += p0 + p1;
+        pk[i] = MmaOp<T>::pack(p0, p1);
+      }
+      l += ls;
+      tmem_st32(tbase + lane_off + b * TC_KB, pk);
+      tc_fence_before();
+      mbar_arrive(&p_full[b]);
+    }
+    // epilogue: O / l -> the row in global memory
+    if (nblk > 0 && !dead && !mbar_wait_bounded(o_done, (nblk - 1) & 1, a.st)) dead = true;
+    dead = __any_sync(0xffffffffu, dead);
+    if (!dead && nblk > 0) {
+      tc_fence_after();
+      uint32_t o[2][32];
+      tmem_ld32(tO + lane_off, o[0]);
+      tmem_ld32(tO + lane_off + 32, o[1]);
+      if (T* orow = out_row(r)) {
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const int e = c * 8;
+          uint4 v;
+          v.x = MmaOp<T>::pack(__uint_as_float(o[e >> 5][e & 31]) * inv, __uint_as_float(o[e >> 5][(e & 31) + 1]) * inv);
+          v.y = MmaOp<T>::pack(__uint_as_float(o[e >> 5][(e & 31) + 2]) * inv, __uint_as_float(o[e >> 5][(e & 31) + 3]) * inv);
+          v.z = MmaOp<T>::pack(__uint_as_float(o[e >> 5][(e & 31) + 4]) * inv, __uint_as_float(o[e >> 5][(e & 31) + 5]) * inv);
+          v.w = MmaOp<T>::pack(__uint_as_float(o[e >> 5][(e & 31) + 6]) * inv, __uint_as_float(o[e >> 5][(e & 31) + 7]) * inv);
+          reinterpret_cast<uint4*>(orow)[c] = v;
+        }
+      }
+    }
+  }
+
+  // ---- free tensor memory once every role is done with it
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tbase), "r"(TC_TMEM_COLS)
+                 : "memory");
+  }
+}
+
+size_t tc_smem() { return 1024 + TC_QTILE + size_t(TC_NST) * TC_STAGE + 256; }
+
+template <typename T, int G>
+int launch_tc_t(const pkv_pool& p, const CUtensorMap& tm, const TcArgs& a, int grid, cudaStream_t s) {
+  static std::mutex mu;
+  static std::vector<char> ready;
+  int dev = 0;
+  PKV_CUDA_RET(cudaGetDevice(&dev));
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if ((int)ready.size() <= dev) ready.resize(dev + 1, 0);
+    if (!ready[dev]) {
+      PKV_CUDA_RET(cudaFuncSetAttribute(prefill_tc_kernel<T, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        int(tc_smem())));
+      ready[dev] = 1;
+    }
+  }
+  prefill_tc_kernel<T, G><<<grid, TC_THREADS, tc_smem(), s>>>(tm, a);
+  PKV_CUDA_RET(cudaGetLastError());
+  return PKV_OK;
+}
+
+template <typename T>
+int launch_tc_g(const pkv_pool& p, int groups, const CUtensorMap& tm, const TcArgs& a, int grid, cudaStream_t s) {
+  switch (groups) {
+    case 1: return launch_tc_t<T, 1>(p, tm, a, grid, s);
+    case 2: return launch_tc_t<T, 2>(p, tm, a, grid, s);
+    case 4: return launch_tc_t<T, 4>(p, tm, a, grid, s);
+    case 8: return launch_tc_t<T, 8>(p, tm, a, grid, s);
+  }
+  return fail(PKV_ERR_UNSUPPORTED, "tcgen05 prefill kernel: unsupported GQA group size");
+}
+
+}  // namespace
+
+int prefill_tc_tile_tokens(int n_heads, int n_kv_heads) { return TC_ROWS / (n_heads / n_kv_heads); }
+
+int prefill_tc_attend(const pkv_pool& p, int layer, int n_heads, const void* q, void* out, float scale,
+                      const pkv_batch& b, const int2* tiles, const int32_t* n_tiles, int64_t tiles_cap,
+                      cudaStream_t s) {
+  if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(out)) & 15)
+    return fail(PKV_ERR_ARG, "q and out must be 16-byte aligned");
+  CUtensorMap tm;
+  if (int rc = pool_tmap_head(p, &tm)) return rc;
+  TcArgs a;
+  a.q = q;
+  a.out = out;
+  a.cu_q = b.cu_query_lens;
+  a.kv_lens = b.kv_lens;
+  a.kv_indptr = b.kv_indptr;
+  a.kv_indices = b.kv_indices;
+  a.last_page_len = b.kv_last_page_len;
+  a.tiles = tiles;
+  a.n_tiles = n_tiles;
+  a.st = b.dev_status;
+  a.num_blocks = p.num_blocks;
+  a.total_pages = b.total_pages;
+  a.n_seqs = b.n_seqs;
+  a.n_tokens = b.n_tokens;
+  a.n_heads = n_heads;
+  a.n_kv = p.n_kv_heads;
+  a.layer = layer;
+  a.scale_log2 = scale * 1.4426950408889634f;
+  const int qt = prefill_tc_tile_tokens(n_heads, p.n_kv_heads);
+  const int64_t bound = std::min<int64_t>((int64_t(b.n_tokens) + qt - 1) / qt + b.n_seqs, tiles_cap);
+  const int64_t grid = std::max<int64_t>(1, bound) * p.n_kv_heads;
+  if (grid > 0x7fffffff) return fail(PKV_ERR_ARG, "prefill batch too large for one launch");
+  const int groups = n_heads / p.n_kv_heads;
+  if (p.dtype == PKV_F16) return launch_tc_g<__half>(p, groups, tm, a, int(grid), s);
+  return launch_tc_g<__nv_bfloat16>(p, groups, tm, a, int(grid), s);
+}
+
+}  // namespace pkv
