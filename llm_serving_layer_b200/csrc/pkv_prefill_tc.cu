@@ -125,6 +125,18 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
       : "r"(taddr)
       : "memory");
 }
+// 64 consecutive 32-bit TMEM columns (two loads, one wait).
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, uint32_t (&r)[64]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%64];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,"
+      "%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%65];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : PKV_R8(0), PKV_R8(8), PKV_R8(16), PKV_R8(24), PKV_R8(32), PKV_R8(40), PKV_R8(48), PKV_R8(56)
+      : "r"(taddr), "r"(taddr + 32)
+      : "memory");
+}
 // 32 consecutive 32-bit TMEM columns of this thread's lane <- r; waits for the store.
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
   asm volatile(
@@ -156,8 +168,8 @@ __global__ void __launch_bounds__(TC_THREADS, 2) prefill_tc_kernel(const __grid_
   uint64_t* empty = full + TC_NST;             // P.V of the stage's block completed
   uint64_t* s_full = empty + TC_NST;           // [2] S block in TMEM
   uint64_t* p_full = s_full + 2;               // [2] P in TMEM (and O rescaled), 128 arrivals
-  uint64_t* o_done = p_full + 2;               // one phase per P.V block
-  uint64_t* q_ready = o_done + 1;              // Q tile in shared memory, 128 arrivals
+  uint64_t* o_done = p_full + 2;               // [2] P.V of block jp done: o_done[jp & 1]
+  uint64_t* q_ready = o_done + 2;              // Q tile in shared memory, 128 arrivals
   uint64_t* drain = q_ready + 1;               // every MMA of the CTA completed
   __shared__ uint32_t s_tmem;
   __shared__ int s_bad;
@@ -202,7 +214,8 @@ __global__ void __launch_bounds__(TC_THREADS, 2) prefill_tc_kernel(const __grid_
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 128);
     }
-    mbar_init(o_done, 1);
+    mbar_init(&o_done[0], 1);
+    mbar_init(&o_done[1], 1);
     mbar_init(q_ready, 128);
     mbar_init(drain, 1);
     fence_mbar_init();
@@ -312,7 +325,7 @@ __global__ void __launch_bounds__(TC_THREADS, 2) prefill_tc_kernel(const __grid_
 #pragma unroll
           for (int k = 0; k < TC_KB / 16; ++k)
             umma_ts(tO, aP + 8 * k, sw128_desc(vaddr + 16 * 128 * k), idPV, (jp > 0 || k > 0) ? 1u : 0u);
-          umma_commit(o_done);
+          umma_commit(&o_done[jp & 1]);
           umma_commit(&empty[stp]);
         }
         __syncwarp();
@@ -346,29 +359,40 @@ __global__ void __launch_bounds__(TC_THREADS, 2) prefill_tc_kernel(const __grid_
     const float sl2 = a.scale_log2;
     float m = -INFINITY, l = 0.f;
     bool dead = false;
+    // Waits on o_done[x] happen in phase order on each barrier: block j always
+    // waits for P.V of block j - 2 (its P buffer is about to be overwritten) and,
+    // only when it rescales O, for P.V of block j - 1 — so a try_wait on a
+    // parity never meets a barrier two phases ahead.
     for (int j = 0; j < nblk; ++j) {
       const int b = j & 1;
       if (!mbar_wait_bounded(&s_full[b], (j >> 1) & 1, a.st)) dead = true;
-      // O may be rescaled (and P overwritten next round) only after the previous P.V
-      if (j >= 1 && !dead && !mbar_wait_bounded(o_done, (j - 1) & 1, a.st)) dead = true;
+      if (j >= 2 && !dead && !mbar_wait_bounded(&o_done[b], ((j - 2) >> 1) & 1, a.st)) dead = true;
       dead = __any_sync(0xffffffffu, dead);
       if (dead) break;
       tc_fence_after();
-      uint32_t sr[2][32];
-      tmem_ld32(tbase + lane_off + b * TC_KB, sr[0]);
-      tmem_ld32(tbase + lane_off + b * TC_KB + 32, sr[1]);
+      uint32_t sr[64];
+      tmem_ld64(tbase + lane_off + b * TC_KB, sr);
       const int kb0 = j * TC_KB;
-      const bool tail = kb0 + TC_KB - 1 > lim;
-      float mx = -INFINITY;
+      if (sl2 <= 0.f) {  // a non-positive scale: scale first so the masked -inf stays the minimum
 #pragma unroll
-      for (int hf = 0; hf < 2; ++hf)
+        for (int i = 0; i < 64; ++i) sr[i] = __float_as_uint(__uint_as_float(sr[i]) * sl2);
+      }
+      if (kb0 + TC_KB - 1 > lim) {  // the block reaches past this row's last visible key
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          float x = __uint_as_float(sr[hf][i]) * sl2;
-          if (tail && kb0 + hf * 32 + i > lim) x = -INFINITY;
-          sr[hf][i] = __float_as_uint(x);
-          mx = fmaxf(mx, x);
-        }
+        for (int i = 0; i < 64; ++i)
+          if (kb0 + i > lim) sr[i] = __float_as_uint(-INFINITY);
+      }
+      float mx;
+      {
+        float t[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) t[u] = __uint_as_float(sr[u]);
+#pragma unroll
+        for (int i = 8; i < 64; ++i) t[i & 7] = fmaxf(t[i & 7], __uint_as_float(sr[i]));
+        mx = fmaxf(fmaxf(fmaxf(t[0], t[1]), fmaxf(t[2], t[3])), fmaxf(fmaxf(t[4], t[5]), fmaxf(t[6], t[7])));
+      }
+      const float sc = sl2 > 0.f ? sl2 : 1.f;  // the scale still to apply (log2 units)
+      mx = mx * sc;                            // -inf stays -inf (sc > 0)
       const float mn = fmaxf(m, mx);
       float m_new = m;
       if (mn != -INFINITY && (m == -INFINITY || mn > m + TC_RESCALE)) m_new = mn;
@@ -377,6 +401,11 @@ __global__ void __launch_bounds__(TC_THREADS, 2) prefill_tc_kernel(const __grid_
       l *= alpha;
       m = m_new;
       if (__any_sync(0xffffffffu, resc)) {
+        // O holds P.V up to block j - 1: let that finish before reading it
+        if (j >= 1 && !mbar_wait_bounded(&o_done[(j - 1) & 1], ((j - 1) >> 1) & 1, a.st)) dead = true;
+        dead = __any_sync(0xffffffffu, dead);
+        if (dead) break;
+        tc_fence_after();
 #pragma unroll
         for (int hf = 0; hf < 2; ++hf) {
           uint32_t o[32];
@@ -387,23 +416,26 @@ __global__ void __launch_bounds__(TC_THREADS, 2) prefill_tc_kernel(const __grid_
         }
       }
       const float mu = m == -INFINITY ? 0.f : m;
-      float ls = 0.f;
+      float lt[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) lt[u] = 0.f;
       uint32_t pk[32];
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
-        const int e = 2 * i;
-        const float p0 = ex2(__uint_as_float(sr[e >> 5][e & 31]) - mu);
-        const float p1 = ex2(__uint_as_float(sr[(e + 1) >> 5][(e + 1) & 31]) - mu);
-        ls += p0 + p1;
+        const float p0 = ex2(fmaf(__uint_as_float(sr[2 * i]), sc, -mu));
+        const float p1 = ex2(fmaf(__uint_as_float(sr[2 * i + 1]), sc, -mu));
+        lt[i & 7] += p0 + p1;
         pk[i] = MmaOp<T>::pack(p0, p1);
       }
+      const float ls = ((lt[0] + lt[1]) + (lt[2] + lt[3])) + ((lt[4] + lt[5]) + (lt[6] + lt[7]));
       l += ls;
       tmem_st32(tbase + lane_off + b * TC_KB, pk);
       tc_fence_before();
       mbar_arrive(&p_full[b]);
     }
-    // epilogue: O / l -> the row in global memory
-    if (nblk > 0 && !dead && !mbar_wait_bounded(o_done, (nblk - 1) & 1, a.st)) dead = true;
+    // epilogue: O / l -> the row in global memory (P.V of the last block done;
+    // the barrier's previous phase was waited at block nblk - 1)
+    if (nblk > 0 && !dead && !mbar_wait_bounded(&o_done[(nblk - 1) & 1], ((nblk - 1) >> 1) & 1, a.st)) dead = true;
     dead = __any_sync(0xffffffffu, dead);
     if (!dead && nblk > 0) {
       tc_fence_after();
