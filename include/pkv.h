@@ -109,12 +109,15 @@ PKV_API int pkv_append_kv(const pkv_pool* pool, int32_t layer, const void* k, co
  * h / (n_heads / n_kv_heads), bottom-right causal limit kv_len - q_len + j.
  * q, out: device [n_tokens][n_heads][head_dim] in the pool dtype.
  *
- * `decode_hint` != 0 selects the split-K decode kernel, which requires every
+ * `decode_hint` 1 selects the split-K decode kernel, which requires every
  * query length to be 1 (checked on the device: PKV_DEV_QLEN_BAD). Otherwise a
  * batch with n_tokens != n_seqs (chunked prefill, prefill mixed with decode
  * tokens) runs the tensor-core prefill kernel when the geometry allows (the
  * decode kernel's: fp16/bf16, head_dim 64, 16-token pages, <= 8 KV heads,
- * 1/2/4/8 query heads per KV head), else the generic kernel. Workspace
+ * 1/2/4/8 query heads per KV head), else the generic kernel; with
+ * `decode_hint` 0 the batch's q_len == 1 rows run on the decode kernel (a
+ * second launch; the plan lists them), with `decode_hint` 2 the caller
+ * asserts there are none and that launch is skipped. Workspace
  * (device, 256-byte aligned) of at least pkv_attend_workspace_size() bytes must
  * be given; its counters must be zero before the first call on it and are left
  * zero by every call. */
@@ -132,7 +135,8 @@ PKV_API int pkv_attend(const pkv_pool* pool, int32_t layer, int32_t n_heads, con
  * first (nothing when only the generic kernel takes the batch). pkv_attend is
  * pkv_plan followed by pkv_attend_planned; a caller attending every layer of
  * one step plans once. The workspace size for a non-decode step is
- * pkv_attend_workspace_size(..., decode_hint = 0). */
+ * pkv_attend_workspace_size(..., decode_hint = 0). A non-decode plan also
+ * lists the batch's q_len == 1 rows for the decode kernel. */
 PKV_API int pkv_plan(const pkv_pool* pool, int32_t n_heads, const pkv_batch* batch, void* workspace,
              size_t workspace_bytes, void* stream);
 PKV_API int pkv_attend_planned(const pkv_pool* pool, int32_t layer, int32_t n_heads, const void* q,

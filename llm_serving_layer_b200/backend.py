@@ -226,7 +226,7 @@ class B200PagedBackend:
         self.last_kernel = st["kernel"]
         N.check(self._lib.pkv_attend_planned(
             self._pdesc, layer_idx, self.n_heads, q.data_ptr(), out.data_ptr(), float(scale),
-            ctypes.byref(st["batch"]), int(st["decode"]), st["ws_ptr"], st["ws_bytes"],
+            ctypes.byref(st["batch"]), st["hint"], st["ws_ptr"], st["ws_bytes"],
             N.stream_ptr(self.device)), "attend")
         return out
 
@@ -257,11 +257,15 @@ class B200PagedBackend:
         total_pages = int(meta.kv_indices.shape[0])
         if n <= 0:
             raise ValueError("BatchMeta has no sequences")
+        # hint for the attention entry point: 1 = every query length is 1 (decode
+        # kernel), 2 = none is (pure prefill), 0 = unknown / mixed (the q_len == 1
+        # rows of a mixed batch run on the decode kernel)
         if self.validate == "host":
-            decode = self._host_validate(meta, n, total_pages)
+            decode, hint = self._host_validate(meta, n, total_pages)
         else:
             mql = getattr(meta, "max_query_len", None)
             decode = (int(mql) == 1) if mql is not None else not bool(meta.is_prefill)
+            hint = 1 if decode else 0
         if decode and n_tokens != n:
             raise ValueError(
                 f"BatchMeta describes a decode step (is_prefill=False) but has {n_tokens} tokens for "
@@ -282,7 +286,7 @@ class B200PagedBackend:
         if self._ws is None or self._ws.numel() < need:
             self._ws = torch.zeros(max(need, 1 << 20), dtype=torch.uint8, device=self.device)
         ws_ptr, ws_bytes = self._ws.data_ptr(), self._ws.numel()
-        kernel = int(self._lib.pkv_attend_kernel(self._pdesc, self.n_heads, n, n_tokens, int(decode)))
+        kernel = int(self._lib.pkv_attend_kernel(self._pdesc, self.n_heads, n, n_tokens, hint))
         if kernel < 0:
             N.check(-kernel, "attend")
         if n_tokens > 0 and (decode or kernel == N.PKV_KERNEL_PREFILL):
@@ -290,14 +294,15 @@ class B200PagedBackend:
                                        N.stream_ptr(self.device)), "plan")
             self.n_plans += 1
         self._meta = meta
-        self._meta_state = {"batch": batch, "tensors": t, "decode": decode, "n_tokens": n_tokens,
+        self._meta_state = {"batch": batch, "tensors": t, "decode": decode, "hint": hint, "n_tokens": n_tokens,
                             "ws_ptr": ws_ptr, "ws_bytes": ws_bytes, "kernel": N.KERNEL_NAMES[kernel]}
         return self._meta_state
 
-    def _host_validate(self, meta: Any, n: int, total_pages: int) -> bool:
+    def _host_validate(self, meta: Any, n: int, total_pages: int) -> tuple[bool, int]:
         """The reference's page-table checks (``paged_torch.py:379-392``) and
         FlashInfer's ``is_prefill`` cross-check (``flashinfer_backend.py:604-618``),
-        once per step. Returns True for a pure-decode step."""
+        once per step. Returns (pure decode step, attention hint: 1 all q_len == 1,
+        2 none, 0 mixed)."""
         ql = meta.query_lens.tolist()
         ip = meta.kv_indptr.tolist()
         lp = meta.kv_last_page_len.tolist()
@@ -332,7 +337,9 @@ class B200PagedBackend:
                 f"BatchMeta.is_prefill={meta.is_prefill} disagrees with query_lens (max={max(ql)}); "
                 "is_prefill must be True iff some sequence contributes more than one token"
             )
-        return not use_prefill
+        if not use_prefill:
+            return True, 1
+        return False, (0 if any(x == 1 for x in ql) else 2)
 
     def invalidate_plan(self) -> None:
         """Forget the cached per-step state (for a caller that mutates a

@@ -53,6 +53,8 @@ struct WsLayout {
   size_t partial_o = 0;   // float[2 * grid][n_heads][D]
   size_t partial_ml = 0;  // float2[2 * grid][n_heads]
   size_t n_tiles = 0;     // int32: prefill tiles planned (prefill layout only)
+  size_t p_dec = 0;       // int64: decode-row pages listed in a mixed batch (prefill layout only)
+  size_t rows = 0;        // int32[n_seqs]: their q / out rows (prefill layout only)
   size_t tiles = 0;       // int2[tiles_cap] {seq, first token} (prefill layout only)
   size_t total = 0;
 };
@@ -76,6 +78,10 @@ WsLayout ws_layout(int n_heads, int n_seqs, int64_t total_pages, int max_grid, i
   if (tiles_cap > 0) {
     w.n_tiles = off;
     off = align256(off + sizeof(int32_t));
+    w.p_dec = off;
+    off = align256(off + sizeof(int64_t));
+    w.rows = off;
+    off = align256(off + sizeof(int32_t) * size_t(std::max(n_seqs, 1)));
     w.tiles = off;
     off = align256(off + sizeof(int2) * size_t(tiles_cap));
   }
@@ -133,8 +139,11 @@ struct DecodeArgs {
   float2* partial_ml;  // [2 * grid][n_heads]      (m, l) of each split piece
   int32_t* counters;
   int32_t* st;
-  int64_t total_pages;
+  const int32_t* rows;   // q / out row of each listed sequence (NULL: row == sequence index)
+  const int64_t* p_dev;  // pages listed, read on the device (NULL: total_pages)
+  int64_t total_pages;   // capacity of desc (and the page count when p_dev is NULL)
   int n_seqs;
+  int n_rows;            // rows of q / out
   int n_heads;
   int layer;
   float scale_log2;
@@ -165,15 +174,15 @@ __device__ __forceinline__ void load_q_frag(const T* __restrict__ q, int row, in
   }
 }
 
-// Warp h merges the split-K pieces in CTAs cf..cl of sequence `seq` for its
-// query heads h*GROUPS .. h*GROUPS + GROUPS - 1. Its own piece (CTA `own`) is
+// Warp h merges the split-K pieces in CTAs cf..cl of a sequence (output row
+// `row`) for its query heads h*GROUPS .. h*GROUPS + GROUPS - 1. Its own piece (CTA `own`) is
 // still in `ostage` (O/l, fp32, [GROUPS][64]) with (m, l) given per lane for
 // the head its elements belong to; every other piece's O/l and (m, l) are read
 // from the workspace, DK_WMERGE pieces per round of loads. Pieces are folded in
 // CTA order with weights l * 2^(m - M) whichever warp merges, so the result is
 // the same bits run after run. Lane `lane` owns elements [lane*PER, lane*PER + PER).
 template <typename T, int GROUPS>
-__device__ __forceinline__ void merge_warp(const DecodeArgs& a, int seq, int h, int own, int64_t fa,
+__device__ __forceinline__ void merge_warp(const DecodeArgs& a, int row, int h, int own, int64_t fa,
                                            int cf, int cl, int64_t P, int G, const float* ostage,
                                            float om, float ol, int lane) {
   constexpr int PER = GROUPS * DK_D / 32;  // 2, 4, 8 or 16 elements per lane
@@ -226,7 +235,7 @@ __device__ __forceinline__ void merge_warp(const DecodeArgs& a, int seq, int h, 
     }
   }
   const float inv = 1.f / W;
-  T* dst = static_cast<T*>(a.out) + (int64_t(seq) * nh + h * GROUPS) * DK_D + e0;
+  T* dst = static_cast<T*>(a.out) + (int64_t(row) * nh + h * GROUPS) * DK_D + e0;
   uint32_t pk[PER / 2];
 #pragma unroll
   for (int r = 0; r < PER; r += 2) pk[r / 2] = MmaOp<T>::pack(acc[r] * inv, acc[r + 1] * inv);
@@ -349,9 +358,14 @@ __global__ void __maxnreg__(DK_MAXNREG) decode_kernel(const __grid_constant__ CU
   uint64_t* empty = full + NST;
   float* ostage_all = reinterpret_cast<float*>(smem + size_t(NST) * STAGE + bar_bytes(2, NST));
 
-  const int64_t P = a.total_pages;
-  const int G = gridDim.x;
+  // pages to cover: the decode rows of a mixed batch are listed by the plan on
+  // the device, so their count is read here (bounded by the descriptor capacity)
+  // The ranges are cut over G = min(grid, P) CTAs, so every range is non-empty
+  // (a split sequence's pieces are exactly the CTAs cf..cl); surplus CTAs exit.
+  const int64_t P = a.p_dev ? max(int64_t(0), min(*a.p_dev, a.total_pages)) : a.total_pages;
+  const int G = int(min(int64_t(gridDim.x), P));
   const int c = blockIdx.x;
+  if (c >= G) return;
   const int64_t p0 = int64_t(c) * P / G, p1 = int64_t(c + 1) * P / G;
   if (p0 >= p1) return;
   const int R = int(p1 - p0);
@@ -463,7 +477,8 @@ __global__ void __maxnreg__(DK_MAXNREG) decode_kernel(const __grid_constant__ CU
   };
 
   uint32_t qb[4][2], qn[4][2];
-  int nxt_seq = -1;
+  int nxt_seq = -1, nxt_row = -1;
+  auto row_of = [&](int sq) -> int { return a.rows ? __ldg(a.rows + sq) : sq; };
   const int first_seq = dfirst.y >> 7;  // its piece (if split) uses partial slot 0
   const int k_tok = (lane & 7) + ((lane >> 3) & 1) * 8, k_chk = lane >> 4;
   const int v_tok = (lane & 7) + (lane >> 4) * 8, v_chk = (lane >> 3) & 1;
@@ -473,7 +488,8 @@ __global__ void __maxnreg__(DK_MAXNREG) decode_kernel(const __grid_constant__ CU
     slide_to(i);
     const int4 d = desc_at(i);
     const int seq = d.y >> 7;
-    if (seq < 0 || seq >= a.n_seqs || (d.y & 31) < 1 || (d.y & 31) > DK_P) {
+    const int row = (seq >= 0 && seq < a.n_seqs) ? (seq == nxt_seq ? nxt_row : row_of(seq)) : -1;
+    if (row < 0 || row >= a.n_rows || (d.y & 31) < 1 || (d.y & 31) > DK_P) {
       // a page of a sequence the plan rejected: drain and release its stage
       if (lane == 0 && !dead) flag(a.st, PKV_DEV_META_BAD);
       wait_full(i);
@@ -490,11 +506,13 @@ __global__ void __maxnreg__(DK_MAXNREG) decode_kernel(const __grid_constant__ CU
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks) { qb[ks][0] = qn[ks][0]; qb[ks][1] = qn[ks][1]; }
     } else {
-      load_q_frag<T, GROUPS>(q, seq, a.n_heads, h, g, c4, qb);
+      load_q_frag<T, GROUPS>(q, row, a.n_heads, h, g, c4, qb);
     }
     // the sequence processed next: H's after T, then each M in turn
     nxt_seq = (i < lenT) ? (dfirst.y >> 7) : seq + 1;
-    if (nxt_seq < a.n_seqs) load_q_frag<T, GROUPS>(q, nxt_seq, a.n_heads, h, g, c4, qn);
+    nxt_row = (nxt_seq >= 0 && nxt_seq < a.n_seqs) ? row_of(nxt_seq) : -1;
+    if (nxt_row >= 0 && nxt_row < a.n_rows) load_q_frag<T, GROUPS>(q, nxt_row, a.n_heads, h, g, c4, qn);
+    else nxt_seq = -1;
     float o[4][4];
 #pragma unroll
     for (int mt = 0; mt < 4; ++mt)
@@ -558,7 +576,7 @@ __global__ void __maxnreg__(DK_MAXNREG) decode_kernel(const __grid_constant__ CU
     __syncwarp();
     if (seen_first && ends_here) {
       // the whole sequence lives in this CTA: store it in the pool dtype
-      T* dst = out + (int64_t(seq) * a.n_heads + h * GROUPS) * DK_D;
+      T* dst = out + (int64_t(row) * a.n_heads + h * GROUPS) * DK_D;
       for (int e = lane * 8; e < GROUPS * DK_D; e += 32 * 8) {
         const float4 x = *reinterpret_cast<const float4*>(ostage + e);
         const float4 y = *reinterpret_cast<const float4*>(ostage + e + 4);
@@ -597,7 +615,7 @@ __global__ void __maxnreg__(DK_MAXNREG) decode_kernel(const __grid_constant__ CU
       const int jh = (lane * GROUPS * DK_D / 32) / DK_D;
       const float mA = __shfl_sync(0xffffffffu, m0, jh >> 1), mB = __shfl_sync(0xffffffffu, m1, jh >> 1);
       const float lA = __shfl_sync(0xffffffffu, lt0, jh >> 1), lB = __shfl_sync(0xffffffffu, lt1, jh >> 1);
-      merge_warp<T, GROUPS>(a, seq, h, c, fa, cf, cl, P, G, ostage, (jh & 1) ? mB : mA, (jh & 1) ? lB : lA, lane);
+      merge_warp<T, GROUPS>(a, row, h, c, fa, cf, cl, P, G, ostage, (jh & 1) ? mB : mA, (jh & 1) ? lB : lA, lane);
       if (lane == 0) *cnt = 0;
     }
     __syncwarp();
@@ -935,7 +953,7 @@ using namespace pkv;
 
 extern "C" size_t pkv_attend_workspace_size(const pkv_pool* pool, int32_t n_heads, int32_t n_seqs,
                                             int64_t total_pages, int32_t decode_hint) {
-  return step_layout(pool, n_heads, n_seqs, total_pages, decode_hint != 0).total;
+  return step_layout(pool, n_heads, n_seqs, total_pages, decode_hint == 1).total;
 }
 
 extern "C" int pkv_plan(const pkv_pool* pool, int32_t n_heads, const pkv_batch* batch,
@@ -948,10 +966,14 @@ extern "C" int pkv_plan(const pkv_pool* pool, int32_t n_heads, const pkv_batch* 
   if (!workspace || workspace_bytes < w.total)
     return fail(PKV_ERR_ARG, "workspace too small: need " + std::to_string(w.total) + " bytes");
   char* ws = static_cast<char*>(workspace);
-  if (!decode)
+  if (!decode) {
+    // a mixed batch's q_len == 1 rows go to the decode kernel when it takes the geometry
+    PrefillMixedPlan mp{reinterpret_cast<int4*>(ws + w.page_desc), reinterpret_cast<int32_t*>(ws + w.counters),
+                        reinterpret_cast<int32_t*>(ws + w.rows), reinterpret_cast<int64_t*>(ws + w.p_dec)};
     return prefill_plan(*pool, n_heads, *batch, reinterpret_cast<int2*>(ws + w.tiles),
                         reinterpret_cast<int32_t*>(ws + w.n_tiles), prefill_tiles_cap(batch->n_seqs, batch->total_pages),
-                        static_cast<cudaStream_t>(stream));
+                        decode_supported(*pool, n_heads) ? &mp : nullptr, static_cast<cudaStream_t>(stream));
+  }
   // every descriptor starts as "no sequence" (-1): pages of a sequence the
   // plan rejects are skipped by the decode kernel instead of read as garbage
   PKV_CUDA_RET(cudaMemsetAsync(ws + w.page_desc, 0xff, sizeof(int4) * size_t(batch->total_pages),
@@ -982,7 +1004,7 @@ extern "C" int pkv_attend_planned(const pkv_pool* pool, int32_t layer, int32_t n
   if (batch->n_tokens == 0) return PKV_OK;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
 
-  if (decode_hint && decode_supported(p, n_heads)) {
+  if (decode_hint == 1 && decode_supported(p, n_heads)) {
     if (batch->n_tokens != batch->n_seqs)
       return fail(PKV_ERR_ARG, "decode: n_tokens must equal n_seqs (one query per sequence)");
     if (batch->total_pages == 0) return fail(PKV_ERR_ARG, "decode: empty page table");
@@ -1003,8 +1025,11 @@ extern "C" int pkv_attend_planned(const pkv_pool* pool, int32_t layer, int32_t n
     a.partial_ml = reinterpret_cast<float2*>(ws + w.partial_ml);
     a.counters = reinterpret_cast<int32_t*>(ws + w.counters);
     a.st = batch->dev_status;
+    a.rows = nullptr;
+    a.p_dev = nullptr;
     a.total_pages = batch->total_pages;
     a.n_seqs = batch->n_seqs;
+    a.n_rows = batch->n_tokens;
     a.n_heads = n_heads;
     a.layer = layer;
     a.scale_log2 = scale * 1.4426950408889634f;
@@ -1013,11 +1038,39 @@ extern "C" int pkv_attend_planned(const pkv_pool* pool, int32_t layer, int32_t n
     return launch_decode_g<__nv_bfloat16>(p, groups, tm, a, batch->total_pages, s);
   }
 
-  if (!decode_hint && batch->n_tokens != batch->n_seqs && prefill_supported(p, n_heads)) {
+  if (decode_hint != 1 && batch->n_tokens != batch->n_seqs && prefill_supported(p, n_heads)) {
     const WsLayout w = step_layout(pool, n_heads, batch->n_seqs, batch->total_pages, false);
     if (!workspace || workspace_bytes < w.total)
       return fail(PKV_ERR_ARG, "workspace too small: need " + std::to_string(w.total) + " bytes");
     char* ws = static_cast<char*>(workspace);
+    if (decode_hint != 2 && decode_supported(p, n_heads) && batch->total_pages > 0) {
+      // the q_len == 1 rows the plan listed, on the decode kernel
+      if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(out)) & 15)
+        return fail(PKV_ERR_ARG, "q and out must be 16-byte aligned");
+      CUtensorMap tm;
+      if (int rc = get_tmap(p, &tm, p.n_kv_heads)) return rc;
+      DecodeArgs a;
+      a.q = q;
+      a.out = out;
+      a.kv_indptr = batch->kv_indptr;
+      a.desc = reinterpret_cast<const int4*>(ws + w.page_desc);
+      a.partial_o = reinterpret_cast<float*>(ws + w.partial_o);
+      a.partial_ml = reinterpret_cast<float2*>(ws + w.partial_ml);
+      a.counters = reinterpret_cast<int32_t*>(ws + w.counters);
+      a.st = batch->dev_status;
+      a.rows = reinterpret_cast<const int32_t*>(ws + w.rows);
+      a.p_dev = reinterpret_cast<const int64_t*>(ws + w.p_dec);
+      a.total_pages = batch->total_pages;
+      a.n_seqs = batch->n_seqs;
+      a.n_rows = batch->n_tokens;
+      a.n_heads = n_heads;
+      a.layer = layer;
+      a.scale_log2 = scale * 1.4426950408889634f;
+      const int groups = n_heads / p.n_kv_heads;
+      const int rc = p.dtype == PKV_F16 ? launch_decode_g<__half>(p, groups, tm, a, batch->total_pages, s)
+                                        : launch_decode_g<__nv_bfloat16>(p, groups, tm, a, batch->total_pages, s);
+      if (rc) return rc;
+    }
     return prefill_attend(p, layer, n_heads, q, out, scale, *batch, reinterpret_cast<const int2*>(ws + w.tiles),
                           reinterpret_cast<const int32_t*>(ws + w.n_tiles),
                           prefill_tiles_cap(batch->n_seqs, batch->total_pages), s);
@@ -1062,16 +1115,16 @@ extern "C" int pkv_attend_kernel(const pkv_pool* pool, int32_t n_heads, int32_t 
                                  int32_t decode_hint) {
   if (int rc = check_pool(pool)) return -rc;
   if (n_heads <= 0 || n_heads % pool->n_kv_heads) return -fail(PKV_ERR_ARG, "n_heads must be a positive multiple of n_kv_heads");
-  if (decode_hint && decode_supported(*pool, n_heads)) return PKV_KERNEL_DECODE;
-  if (!decode_hint && n_tokens != n_seqs && prefill_supported(*pool, n_heads)) return PKV_KERNEL_PREFILL;
+  if (decode_hint == 1 && decode_supported(*pool, n_heads)) return PKV_KERNEL_DECODE;
+  if (decode_hint != 1 && n_tokens != n_seqs && prefill_supported(*pool, n_heads)) return PKV_KERNEL_PREFILL;
   return PKV_KERNEL_GENERIC;
 }
 
 extern "C" int pkv_attend(const pkv_pool* pool, int32_t layer, int32_t n_heads, const void* q,
                           void* out, float scale, const pkv_batch* batch, int32_t decode_hint,
                           void* workspace, size_t workspace_bytes, void* stream) {
-  if (pool && batch && ((decode_hint && decode_supported(*pool, n_heads)) ||
-                        (!decode_hint && batch->n_tokens != batch->n_seqs && prefill_supported(*pool, n_heads)))) {
+  if (pool && batch && ((decode_hint == 1 && decode_supported(*pool, n_heads)) ||
+                        (decode_hint != 1 && batch->n_tokens != batch->n_seqs && prefill_supported(*pool, n_heads)))) {
     if (int rc = pkv_plan(pool, n_heads, batch, workspace, workspace_bytes, stream)) return rc;
   }
   return pkv_attend_planned(pool, layer, n_heads, q, out, scale, batch, decode_hint, workspace,
@@ -1194,8 +1247,11 @@ extern "C" int pkv_attend_decode_noalloc(const pkv_pool* pool, int32_t layer, in
   a.partial_ml = reinterpret_cast<float2*>(ws + w.partial_ml);
   a.counters = reinterpret_cast<int32_t*>(ws + w.counters);
   a.st = batch->dev_status;
+  a.rows = nullptr;
+  a.p_dev = nullptr;
   a.total_pages = batch->total_pages;
   a.n_seqs = batch->n_seqs;
+  a.n_rows = batch->n_tokens;
   a.n_heads = n_heads;
   a.layer = layer;
   a.scale_log2 = scale * 1.4426950408889634f;

@@ -59,8 +59,16 @@ int pool_tmap_head(const pkv_pool& p, CUtensorMap* out);
 bool prefill_supported(const pkv_pool& p, int n_heads);
 int prefill_tile_tokens(int n_heads, int n_kv_heads);
 int64_t prefill_tiles_cap(int n_seqs, int64_t total_pages);
+// Where the plan of a mixed batch lists its decode rows for the decode kernel
+// (workspace regions; see pkv_attn.cu's workspace layout).
+struct PrefillMixedPlan {
+  int4* desc;          // [total_pages] page descriptors of the listed decode rows
+  int32_t* counters;   // [n_seqs][8] split-K counters
+  int32_t* rows;       // [n_seqs] q / out row of each listed sequence, -1 past the list
+  int64_t* p_dec;      // pages listed
+};
 int prefill_plan(const pkv_pool& p, int n_heads, const pkv_batch& b, int2* tiles, int32_t* n_tiles,
-                 int64_t tiles_cap, cudaStream_t s);
+                 int64_t tiles_cap, const PrefillMixedPlan* mixed, cudaStream_t s);
 int prefill_attend(const pkv_pool& p, int layer, int n_heads, const void* q, void* out, float scale,
                    const pkv_batch& b, const int2* tiles, const int32_t* n_tiles, int64_t tiles_cap,
                    cudaStream_t s);

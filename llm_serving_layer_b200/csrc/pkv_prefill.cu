@@ -65,14 +65,57 @@ __device__ __forceinline__ int tile_pages(int64_t kv, int ql, int j0, int qt) {
   return int(c < 0x7fffffff ? c : 0x7fffffff);
 }
 
+// Exclusive prefix sum of v over the CTA (every thread calls it); *total gets the sum.
+__device__ __forceinline__ int block_excl_scan(int v, int* warp_sum, int* total) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+  int incl = v;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const int u = __shfl_up_sync(0xffffffffu, incl, off);
+    if (lane >= off) incl += u;
+  }
+  __syncthreads();
+  if (lane == 31) warp_sum[w] = incl;
+  __syncthreads();
+  if (w == 0) {
+    int x = lane < nw ? warp_sum[lane] : 0;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int u = __shfl_up_sync(0xffffffffu, x, off);
+      if (lane >= off) x += u;
+    }
+    warp_sum[lane] = x;
+  }
+  __syncthreads();
+  *total = warp_sum[nw - 1];
+  return (w ? warp_sum[w - 1] : 0) + incl - v;
+}
+
+// Decode rows of a mixed batch, for the decode kernel: the q_len == 1
+// sequences are listed contiguously (index d), their pages get the decode
+// kernel's descriptors {page id, d<<7 | first<<6 | last<<5 | valid, first page
+// of d, one past its last page} in listed order, rows[d] = their q / out row,
+// rows past the list = -1, *p_dec = pages listed; split-K counters zeroed.
+struct MixedOut {
+  const int32_t* kv_indices;
+  const int32_t* kv_lens;
+  int64_t total_pages, num_blocks;
+  int4* desc;
+  int32_t* counters;  // [n_seqs][8]
+  int32_t* rows;      // [n_seqs]
+  int64_t* p_dec;
+};
+
 __global__ void __launch_bounds__(1024) prefill_plan_kernel(
     const int32_t* __restrict__ cu_q, const int32_t* __restrict__ kv_indptr,
     const int32_t* __restrict__ last_page_len, int n_seqs, int n_tokens, int qt, int max_tiles,
-    int2* __restrict__ tiles, int32_t* __restrict__ n_tiles, int32_t* st) {
+    int2* __restrict__ tiles, int32_t* __restrict__ n_tiles, int32_t* st, int mixed, MixedOut mo) {
   __shared__ int cnt[PF_BUCKETS];
   __shared__ int warp_sum[32];
   __shared__ int s_bad, s_total;
   const int tid = threadIdx.x;
+  // in a mixed batch the q_len == 1 sequences go to the decode kernel, not into tiles
+  const int min_ql = mixed ? 2 : 1;
   for (int b = tid; b < PF_BUCKETS; b += blockDim.x) cnt[b] = 0;
   if (tid == 0) {
     s_bad = (cu_q[0] != 0 || cu_q[n_seqs] != n_tokens) ? 1 : 0;
@@ -90,6 +133,7 @@ __global__ void __launch_bounds__(1024) prefill_plan_kernel(
       s_bad = 1;
       continue;
     }
+    if (ql < min_ql) continue;
     const int64_t kv = seq_kv(s);
     atomicAdd(&s_total, (ql + qt - 1) / qt);
     for (int j0 = 0; j0 < ql; j0 += qt) atomicAdd(&cnt[min(tile_pages(kv, ql, j0, qt), PF_BUCKETS - 1)], 1);
@@ -99,6 +143,7 @@ __global__ void __launch_bounds__(1024) prefill_plan_kernel(
     if (tid == 0) {
       flag(st, PKV_DEV_META_BAD);
       *n_tiles = 0;
+      if (mixed) *mo.p_dec = 0;
     }
     return;
   }
@@ -130,6 +175,7 @@ __global__ void __launch_bounds__(1024) prefill_plan_kernel(
   __syncthreads();
   for (int s = tid; s < n_seqs; s += blockDim.x) {
     const int ql = cu_q[s + 1] - cu_q[s];
+    if (ql < min_ql) continue;
     const int64_t kv = seq_kv(s);
     for (int j0 = 0; j0 < ql; j0 += qt) {
       const int pos = atomicAdd(&cnt[min(tile_pages(kv, ql, j0, qt), PF_BUCKETS - 1)], 1);
@@ -137,6 +183,45 @@ __global__ void __launch_bounds__(1024) prefill_plan_kernel(
     }
   }
   if (tid == 0) *n_tiles = s_total;
+  if (!mixed) return;
+
+  // ---- decode rows of the mixed batch, listed in sequence order
+  int base_seq = 0, base_pg = 0;
+  for (int c0 = 0; c0 < n_seqs; c0 += blockDim.x) {
+    const int s = c0 + tid;
+    int isdec = 0, np = 0, lpl = 0;
+    int64_t pa = 0;
+    if (s < n_seqs && cu_q[s + 1] - cu_q[s] == 1) {
+      pa = kv_indptr[s];
+      const int64_t pb = kv_indptr[s + 1];
+      lpl = last_page_len[s];
+      bool bad = pb < pa + 1 || pa < 0 || pb > mo.total_pages || lpl < 1 || lpl > PF_P;
+      if (!bad && mo.kv_lens && int64_t(mo.kv_lens[s]) != (pb - pa - 1) * PF_P + lpl) bad = true;
+      if (bad) flag(st, PKV_DEV_META_BAD);
+      else {
+        isdec = 1;
+        np = int(pb - pa);
+      }
+    }
+    int tot_seq, tot_pg;
+    const int d = base_seq + block_excl_scan(isdec, warp_sum, &tot_seq);
+    const int off = base_pg + block_excl_scan(np, warp_sum, &tot_pg);
+    if (isdec) {
+      mo.rows[d] = cu_q[s];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) mo.counters[size_t(d) * 8 + k] = 0;
+      for (int p = 0; p < np; ++p) {
+        const int id = mo.kv_indices[pa + p];
+        if (id < 0 || id >= mo.num_blocks) flag(st, PKV_DEV_SLOT_OOB);
+        const int first = p == 0, last = p == np - 1;
+        mo.desc[off + p] = make_int4(id, (d << 7) | (first << 6) | (last << 5) | (last ? lpl : PF_P), off, off + np);
+      }
+    }
+    base_seq += tot_seq;
+    base_pg += tot_pg;
+  }
+  for (int d = base_seq + tid; d < n_seqs; d += blockDim.x) mo.rows[d] = -1;
+  if (tid == 0) *mo.p_dec = base_pg;
 }
 
 // ---------------------------------------------------------------- attention
@@ -498,12 +583,23 @@ int64_t prefill_tiles_cap(int n_seqs, int64_t total_pages) {
 }
 
 int prefill_plan(const pkv_pool& p, int n_heads, const pkv_batch& b, int2* tiles, int32_t* n_tiles,
-                 int64_t tiles_cap, cudaStream_t s) {
+                 int64_t tiles_cap, const PrefillMixedPlan* mixed, cudaStream_t s) {
   const int qt = prefill_tile_tokens(n_heads, p.n_kv_heads);
   const int cap = int(std::min<int64_t>(tiles_cap, 0x7fffffff));
+  MixedOut mo{};
+  if (mixed) {
+    mo.kv_indices = b.kv_indices;
+    mo.kv_lens = b.kv_lens;
+    mo.total_pages = b.total_pages;
+    mo.num_blocks = p.num_blocks;
+    mo.desc = mixed->desc;
+    mo.counters = mixed->counters;
+    mo.rows = mixed->rows;
+    mo.p_dec = mixed->p_dec;
+  }
   prefill_plan_kernel<<<1, PF_BUCKETS, 0, s>>>(b.cu_query_lens, b.kv_indptr, b.kv_last_page_len,
                                                b.n_seqs, b.n_tokens, qt, cap, tiles, n_tiles,
-                                               b.dev_status);
+                                               b.dev_status, mixed ? 1 : 0, mo);
   PKV_CUDA_RET(cudaGetLastError());
   return PKV_OK;
 }

@@ -32,14 +32,14 @@ def cuda():
 
 
 def build_step(seed, specs, num_blocks, dtype=torch.float16, Hkv=8, Hq=32, D=64, poison=None,
-               kv_std=0.5 ** 0.5, layers=1):
+               kv_std=0.5 ** 0.5, layers=1, validate="host"):
     """One prefill step over a seeded, scattered pool. ``specs`` lists
     (tokens already cached, tokens in this step's chunk) per sequence: the
     cached prefix is written by one history append, the chunk's K/V by the
     step's own append_kv (as the engine does before attend)."""
     rs = np.random.RandomState(seed)
     alloc = FifoAllocator(num_blocks, 16, order=rs.permutation(num_blocks))
-    bk = B200PagedBackend(layers, num_blocks, 16, Hkv, Hq, D, device="cuda:0", dtype=dtype)
+    bk = B200PagedBackend(layers, num_blocks, 16, Hkv, Hq, D, device="cuda:0", dtype=dtype, validate=validate)
     if poison is not None:
         for l in range(layers):
             bk.k_pool[l].fill_(poison)
@@ -223,3 +223,20 @@ def test_radix_shared_prefix_with_copy_on_write_matches_private_copies():
     assert torch.equal(out_s, out_p)
     err = np.abs(out_s.double().cpu().numpy() - exact(bk_s, q_all.cpu(), m_s, 0.125)).max()
     assert err <= 2e-3
+
+
+@pytest.mark.parametrize("validate", ["host", "device"])
+def test_mixed_batch_decode_rows_take_the_decode_kernel(validate):
+    """A mixed step (decode rows + prefill chunks): the q_len == 1 rows are listed
+    by the plan and run on the decode kernel (a second launch), the rest on the
+    prefill kernel — in device-validate mode too, where the backend cannot see
+    the query lengths. Long decode histories make the decode kernel split them."""
+    rs = np.random.RandomState(77)
+    specs = ([(int(x), 1) for x in rs.randint(1, 2048, 200)] + [(0, 300), (700, 40), (5, 2)]
+             + [(int(x), 1) for x in rs.randint(1, 64, 50)])
+    need = sum((s + q + 15) // 16 for s, q in specs) + 8
+    bk, seqs, m, q = build_step(78, specs, need * 2, validate=validate)
+    out = check(bk, m, q)
+    again = bk.attend(q.cuda(), 0, 0.125, m)
+    torch.cuda.synchronize()
+    assert torch.equal(out, again)
