@@ -1,5 +1,6 @@
 // pkv_abi.cu — library-wide host plumbing: version, per-thread error text,
 // pool validation, device properties.
+#include <cstdlib>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -51,6 +52,14 @@ int num_sms() {
     cache[dev] = n;
   }
   return cache[dev];
+}
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("PKV_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
 }
 
 }  // namespace pkv

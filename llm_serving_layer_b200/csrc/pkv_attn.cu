@@ -360,6 +360,9 @@ __global__ void __maxnreg__(DK_MAXNREG) decode_kernel(const __grid_constant__ CU
 
   // pages to cover: the decode rows of a mixed batch are listed by the plan on
   // the device, so their count is read here (bounded by the descriptor capacity)
+  pdl_trigger();
+  if (threadIdx.x == 0) prefetch_tmap(&tmap);
+  pdl_wait();  // the plan, q and this step's append are written by earlier kernels
   // The ranges are cut over G = min(grid, P) CTAs, so every range is non-empty
   // (a split sequence's pieces are exactly the CTAs cf..cl); surplus CTAs exit.
   const int64_t P = a.p_dev ? max(int64_t(0), min(*a.p_dev, a.total_pages)) : a.total_pages;
@@ -370,7 +373,6 @@ __global__ void __maxnreg__(DK_MAXNREG) decode_kernel(const __grid_constant__ CU
   if (p0 >= p1) return;
   const int R = int(p1 - p0);
   if (threadIdx.x == 0) {
-    prefetch_tmap(&tmap);
     for (int i = 0; i < NST; ++i) {
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], n_cons);
@@ -892,9 +894,8 @@ int launch_decode_t(const pkv_pool& p, const CUtensorMap& tm, DecodeArgs& a, int
   if (limit <= 0) return PKV_ERR_CUDA;  // message already set
   limit = std::min(limit, max_decode_grid());
   const int grid = int(std::max<int64_t>(1, std::min<int64_t>(limit, total_pages)));
-  decode_kernel<T, GROUPS, NST, MINB>
-      <<<grid, 32 * (p.n_kv_heads + 1), decode_smem(p.n_kv_heads, GROUPS, NST), s>>>(tm, a);
-  PKV_CUDA_RET(cudaGetLastError());
+  PKV_CUDA_RET(launch_kernel(decode_kernel<T, GROUPS, NST, MINB>, dim3(grid), dim3(32 * (p.n_kv_heads + 1)),
+                             decode_smem(p.n_kv_heads, GROUPS, NST), s, true, tm, a));
   return PKV_OK;
 }
 

@@ -11,6 +11,7 @@
 #include <stdint.h>
 
 #include <string>
+#include <utility>
 
 #include "../../include/pkv.h"
 
@@ -48,6 +49,28 @@ inline int64_t slab_bytes(const pkv_pool& p) { return block_bytes(p) * p.num_blo
 
 int num_sms();  // SM count of the current device (cached per device)
 
+// Programmatic dependent launch (PDL): the per-layer kernels of a step
+// (append, decode) are launched so that the next one may be scheduled while
+// the previous one drains; each waits (griddepcontrol.wait, a no-op when it was
+// launched without the attribute) before it reads anything an earlier kernel
+// wrote, so stream order still holds for every byte. PKV_PDL=0 turns it off.
+bool pdl_enabled();
+template <typename... KArgs, typename... Args>
+cudaError_t launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                          bool pdl, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = (pdl && pdl_enabled()) ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 // Tensor map of a pool's permuted page view (dims D, token slot, KV head,
 // layer*2+kv; one box = one whole [8 heads][16 tok][64] page of one layer's K
 // or V), cached per (device, pool). pkv_attn.cu.
@@ -79,6 +102,11 @@ int prefill_tc_attend(const pkv_pool& p, int layer, int n_heads, const void* q, 
                       cudaStream_t s);
 
 // ---------------------------------------------------------------- device side
+// PDL: let the next kernel in the stream be scheduled now; wait until the
+// kernels before this one completed and their writes are visible.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 __device__ __forceinline__ void flag(int32_t* st, int32_t bits) {
   if (st) atomicOr(st, bits);
 }

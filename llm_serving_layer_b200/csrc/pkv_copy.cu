@@ -50,6 +50,8 @@ __global__ void __launch_bounds__(256) append_kernel(char* __restrict__ k_slab,
                                                      int64_t n_tokens, int64_t n_slots,
                                                      int64_t row_bytes, int32_t* st) {
   using T = typename Vec<W>::T;
+  pdl_trigger();
+  pdl_wait();  // k, v and slot_mapping may come from the kernels just before
   const int64_t warp = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= 2 * n_tokens) return;
@@ -189,10 +191,10 @@ extern "C" int pkv_append_kv(const pkv_pool* pool, int32_t layer, const void* k,
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const char* kk = static_cast<const char*>(k);
   const char* vv = static_cast<const char*>(v);
-#define PKV_APPEND_CASE(WW)                                                                   \
-  case WW:                                                                                    \
-    append_kernel<WW><<<grid, block, 0, s>>>(k_slab, v_slab, kk, vv, slot_mapping, n_tokens, \
-                                             n_slots, rb, dev_status);                        \
+#define PKV_APPEND_CASE(WW)                                                                       \
+  case WW:                                                                                        \
+    PKV_CUDA_RET(launch_kernel(append_kernel<WW>, grid, block, 0, s, true, k_slab, v_slab, kk, vv, \
+                               slot_mapping, n_tokens, n_slots, rb, dev_status));                 \
     break;
   switch (w) {
     PKV_APPEND_CASE(16)
