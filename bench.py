@@ -6,7 +6,9 @@ layers of Llama-3.2-1B geometry at batch 256.
 
 A step = one decode step of the hot path: for each of the 16 layers, the
 KV-append of one new token per sequence (append_kv) then paged attention over
-the full history (attend). Workload (seeded, synthetic — the reference uses no
+the full history (attend) — the reference engine's two calls; the same step
+with both folded into one launch per layer (B200PagedBackend.append_attend) is
+timed beside it (``fused``). Workload (seeded, synthetic — the reference uses no
 dataset on this path): 256 sequences with context lengths lognormal(mu =
 ln 256 - 0.32, sigma = 0.8) clipped to [1, 2048] (mean ~258, p90 ~524); 16-token
 blocks scattered over a pool of 90% of HBM by a seeded permutation; K, V ~ N(0,
@@ -17,7 +19,8 @@ in HBM (per-step CUDA graphs replayed back to back; each step reads ~2.2 GB of
 KV, far larger than L2, so no flush is needed); ``e2e`` = the same metric
 through the public Python API with host buffers and per-step H2D/D2H inside
 the timed region; ``roofline`` = the decode kernel's algorithmic bytes per
-launch / its CUDA-event-timed average launch duration vs measured HBM peak;
+launch / its CUDA-event-timed average launch duration vs measured HBM peak
+(other legs: config 3 prefill, config 4 swap, config 5 Llama serving);
 ``cpu_baseline`` = the CPU oracle (the reference algorithm restated) on this
 host. Multi-GPU (torchrun): independent replicas, no data-path collective.
 """
@@ -300,8 +303,11 @@ def run_b200(args) -> None:
         bk.plan(m)
         outs = []
         for layer in range(L):
-            bk.append_kv(layer, ks[layer], vs[layer], m)
-            outs.append(bk.attend(qs[layer], layer, SCALE, m))
+            if args.fuse:
+                outs.append(bk.append_attend(layer, ks[layer], vs[layer], qs[layer], SCALE, m))
+            else:
+                bk.append_kv(layer, ks[layer], vs[layer], m)
+                outs.append(bk.attend(qs[layer], layer, SCALE, m))
         return outs
 
     # warm every cache (tensor maps, occupancy, allocator) eagerly, then capture
@@ -326,12 +332,19 @@ def run_b200(args) -> None:
                 torch.cuda.Event(enable_timing=True, external=True))]
         with torch.cuda.graph(gr, pool=pool_handle):
             bk.plan(m)
-            for layer in range(L):
-                bk.append_kv(layer, ks[layer], vs[layer], m)
-            evs[0][0].record()
-            for layer in range(L):
-                bk.attend(qs[layer], layer, SCALE, m)
-            evs[0][1].record()
+            if args.fuse:
+                # append + attend per layer in one launch (B200PagedBackend.append_attend)
+                evs[0][0].record()
+                for layer in range(L):
+                    bk.append_attend(layer, ks[layer], vs[layer], qs[layer], SCALE, m)
+                evs[0][1].record()
+            else:
+                for layer in range(L):
+                    bk.append_kv(layer, ks[layer], vs[layer], m)
+                evs[0][0].record()
+                for layer in range(L):
+                    bk.attend(qs[layer], layer, SCALE, m)
+                evs[0][1].record()
         pool_handle = gr.pool()
         graphs.append(gr)
         ev.append(evs)
@@ -382,8 +395,10 @@ def run_b200(args) -> None:
     for m in metas[args.warmup:]:
         kv = m.kv_lens.sum().item()
         pages_m = int(m.kv_indices.shape[0])
-        # K+V read of every token's row, Q read + O write, one 8-byte page descriptor per page
-        alg.append(kv * HKV * D * 2 * 2 + N_SEQ * HQ * D * 2 * 2 + pages_m * 8)
+        # K+V read of every token's row, Q read + O write, one 8-byte page descriptor per page;
+        # with the append fused in: the new K/V rows read and written to their slots too
+        alg.append(kv * HKV * D * 2 * 2 + N_SEQ * HQ * D * 2 * 2 + pages_m * 8
+                   + (N_SEQ * HKV * D * 2 * 2 * 2 if args.fuse else 0))
     alg_bytes = sum(alg) / len(alg)
     peak, peak_kind = measured_peaks()
     achieved = alg_bytes / (avg_launch_ms / 1e3) / 1e9
@@ -395,6 +410,50 @@ def run_b200(args) -> None:
             traffic = round(float(tj["dram_bytes_per_alg_byte"]) * alg_bytes)
         except Exception:
             traffic = None
+
+    # ---- the same steps with append + attend fused into one launch per layer
+    fused = None
+    if args.fused_extra and not args.fuse:
+        fgraphs, fev = [], []
+        for m in metas[args.warmup:]:
+            bk.invalidate_plan()
+            gr = torch.cuda.CUDAGraph()
+            evf = (torch.cuda.Event(enable_timing=True, external=True),
+                   torch.cuda.Event(enable_timing=True, external=True))
+            with torch.cuda.graph(gr, pool=pool_handle):
+                bk.plan(m)
+                evf[0].record()
+                for layer in range(L):
+                    bk.append_attend(layer, ks[layer], vs[layer], qs[layer], SCALE, m)
+                evf[1].record()
+            fgraphs.append(gr)
+            fev.append(evf)
+        for gr in fgraphs[:3]:
+            gr.replay()
+        torch.cuda.synchronize()
+        fsteps = min(args.steps, 4 * n_graphs)
+        if ws > 1:
+            dist.barrier()
+        e0.record()
+        for s in range(fsteps):
+            fgraphs[s % n_graphs].replay()
+        e1.record()
+        torch.cuda.synchronize()
+        fms = e0.elapsed_time(e1)
+        if ws > 1:
+            t = torch.tensor([fms], device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            fms = float(t.item())
+        bk.check_status()
+        fl = [a.elapsed_time(b) / L for a, b in fev]
+        falg = alg_bytes + N_SEQ * HKV * D * 2 * 2 * 2  # plus the new K/V rows read and written to their slots
+        flaunch = sum(fl) / len(fl)
+        fused = {"value": round(N_SEQ * ws * fsteps / (fms / 1e3), 1), "unit": UNIT, "steps": fsteps,
+                 "ms_per_step": round(fms / fsteps, 4), "avg_launch_us": round(flaunch * 1e3, 2),
+                 "alg_bytes_per_launch": int(falg),
+                 "frac": round(falg / (flaunch / 1e3) / 1e9 / peak, 4),
+                 "path": "B200PagedBackend.append_attend: KV-append folded into the decode kernel (one launch per layer)"}
+        del fgraphs
 
     # ---- e2e: public API, host buffers, H2D + D2H inside the timed region
     e2e = run_e2e(torch, bk, tables, ctx, args, device, ws, dist, n_graphs)
@@ -443,9 +502,11 @@ def run_b200(args) -> None:
                          "peak_kind": peak_kind, "kernel": "decode_kernel",
                          "alg_bytes_per_launch": int(alg_bytes), "avg_launch_us": round(avg_launch_ms * 1e3, 2),
                          "timing": ("CUDA events inside each timed step graph around its 16 back-to-back "
-                                    "decode launches; mean launch = elapsed / 16")},
+                                    "decode launches; mean launch = elapsed / 16"),
+                         "fused_append": bool(args.fuse)},
             "cpu_baseline": cpu_line,
-            "gpu_launches": args.steps * (1 + 2 * L),
+            "gpu_launches": args.steps * (1 + (1 if args.fuse else 2) * L),
+            "fused": fused,
             "clocks": clock_info,
             **line_extra,
         }
@@ -709,17 +770,20 @@ def run_prefill(torch, bk, args, device) -> dict:
         T = int(m.positions.shape[0])
         bk.invalidate_plan()
         gr = torch.cuda.CUDAGraph()
+        # copies, plan and the 16 appends, then the 16 attends back to back inside
+        # one event pair (mean attend launch = elapsed / 16), as in the decode leg
         ev = [(torch.cuda.Event(enable_timing=True, external=True),
-               torch.cuda.Event(enable_timing=True, external=True)) for _ in range(L)]
+               torch.cuda.Event(enable_timing=True, external=True))]
         with torch.cuda.graph(gr, pool=pool_handle):
             for a, b in cw:
                 bk.copy_block(a, b)
             bk.plan(m)
             for layer in range(L):
                 bk.append_kv(layer, kb[layer][:T], vb[layer][:T], m)
-                ev[layer][0].record()
+            ev[0][0].record()
+            for layer in range(L):
                 bk.attend(qb[layer][:T], layer, SCALE, m)
-                ev[layer][1].record()
+            ev[0][1].record()
         pool_handle = gr.pool()
         graphs.append(gr)
         evs.append(ev)
@@ -749,7 +813,8 @@ def run_prefill(torch, bk, args, device) -> dict:
         "ms_total": round(ms, 3), "attn_ms_total": round(attn_ms, 3),
         "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak, "unit": "TFLOP/s",
                      "frac": round(achieved / peak, 4), "peak_kind": peak_kind, "kernel": "prefill_kernel",
-                     "avg_launch_us": round(attn_ms * 1e3 / (len(graphs) * L), 2)},
+                     "avg_launch_us": round(attn_ms * 1e3 / (len(graphs) * L), 2),
+                     "timing": "CUDA events around each step's 16 back-to-back attend launches"},
         "batched_64x512": batched,
     }
     del graphs
@@ -1031,6 +1096,10 @@ def main() -> None:
     ap.add_argument("--no-swap", dest="swap", action="store_false")
     ap.add_argument("--no-prefill", dest="prefill", action="store_false")
     ap.add_argument("--no-llama", dest="llama", action="store_false")
+    ap.add_argument("--fused", dest="fuse", action="store_true",
+                    help="time the fused append_attend step as the main value (default: append_kv + attend, "
+                         "the reference API, with the fused step reported beside it)")
+    ap.add_argument("--no-fused-extra", dest="fused_extra", action="store_false")
     ap.add_argument("--llama-steps", type=int, default=100)
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)

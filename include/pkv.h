@@ -143,6 +143,20 @@ PKV_API int pkv_attend_planned(const pkv_pool* pool, int32_t layer, int32_t n_he
                        void* out, float scale, const pkv_batch* batch, int32_t decode_hint,
                        void* workspace, size_t workspace_bytes, void* stream);
 
+/* KV-append and attention of one layer in one call: pkv_append_kv followed by
+ * pkv_attend_planned, with the same arguments and result. For a decode batch
+ * (decode_hint 1) on the decode kernel's geometry it is ONE launch: the
+ * decode kernel writes each row's new K/V to its slot and patches it into the
+ * staged copy of the sequence's last page, which must be the token's slot
+ * (the last written position of that page, as in every decode step;
+ * PKV_DEV_META_BAD otherwise). Other batches take the two calls. No
+ * counterpart in the reference (its engine calls append_kv then attend per
+ * layer, docs/ARCHITECTURE.md:167-172). */
+PKV_API int pkv_append_attend_planned(const pkv_pool* pool, int32_t layer, int32_t n_heads, const void* k,
+                              const void* v, const int32_t* slot_mapping, const void* q, void* out,
+                              float scale, const pkv_batch* batch, int32_t decode_hint, void* workspace,
+                              size_t workspace_bytes, void* stream);
+
 /* Which kernel pkv_attend_planned runs for a batch of this shape and hint
  * (host only, nothing touches the device): PKV_KERNEL_GENERIC,
  * PKV_KERNEL_DECODE or PKV_KERNEL_PREFILL; -PKV_ERR_ARG for a bad pool. No

@@ -176,6 +176,41 @@ class B200PagedBackend:
     def append_kv(self, layer_idx: int, k: torch.Tensor, v: torch.Tensor, meta: Any) -> None:
         """Scatter this step's K/V into the pool at ``meta.slot_mapping``
         (``paged_torch.py:209-276``). Idempotent."""
+        k, v, slots, tokens = self._append_args(layer_idx, k, v, meta)
+        if tokens == 0:
+            return
+        N.check(self._lib.pkv_append_kv(self._pdesc, layer_idx, k.data_ptr(), v.data_ptr(),
+                                        slots.data_ptr(), tokens, self._status.data_ptr(),
+                                        N.stream_ptr(self.device)), "append_kv")
+
+    def append_attend(self, layer_idx: int, k: torch.Tensor, v: torch.Tensor, q: torch.Tensor,
+                      scale: float, meta: Any) -> torch.Tensor:
+        """``append_kv(layer_idx, k, v, meta)`` then ``attend(q, layer_idx, scale,
+        meta)`` in one call, with the same checks, errors and results. A decode
+        step is ONE kernel launch: the decode kernel writes each sequence's new
+        K/V row to its slot and attends over it (no reference counterpart; the
+        engine makes the two calls, ``docs/ARCHITECTURE.md:167-172``)."""
+        k, v, slots, tokens = self._append_args(layer_idx, k, v, meta)
+        if q.shape != (tokens, self.n_heads, self.head_dim):
+            raise ValueError(
+                f"q has shape {tuple(q.shape)}, expected ({tokens}, {self.n_heads}, {self.head_dim})"
+            )
+        st = self._step_state(meta)
+        if st["n_tokens"] != tokens:
+            raise ValueError(f"meta describes {st['n_tokens']} tokens but q has {tokens}")
+        q = q.to(device=self.device, dtype=self.dtype).contiguous()
+        out = torch.empty_like(q)
+        if tokens == 0:
+            return out
+        self.n_runs += 1
+        self.last_kernel = st["kernel"]
+        N.check(self._lib.pkv_append_attend_planned(
+            self._pdesc, layer_idx, self.n_heads, k.data_ptr(), v.data_ptr(), slots.data_ptr(), q.data_ptr(),
+            out.data_ptr(), float(scale), ctypes.byref(st["batch"]), st["hint"], st["ws_ptr"], st["ws_bytes"],
+            N.stream_ptr(self.device)), "append_attend")
+        return out
+
+    def _append_args(self, layer_idx: int, k: torch.Tensor, v: torch.Tensor, meta: Any):
         self._check_layer(layer_idx)
         if getattr(meta, "slot_mapping", None) is None:
             raise ValueError(
@@ -193,14 +228,10 @@ class B200PagedBackend:
             raise ValueError(
                 f"slot_mapping has {meta.slot_mapping.shape[0]} entries but {tokens} tokens were supplied"
             )
-        if tokens == 0:
-            return
         k = k.to(device=self.device, dtype=self.dtype).contiguous()
         v = v.to(device=self.device, dtype=self.dtype).contiguous()
-        slots = self._i32(meta.slot_mapping)
-        N.check(self._lib.pkv_append_kv(self._pdesc, layer_idx, k.data_ptr(), v.data_ptr(),
-                                        slots.data_ptr(), tokens, self._status.data_ptr(),
-                                        N.stream_ptr(self.device)), "append_kv")
+        slots = self._i32(meta.slot_mapping) if tokens else None
+        return k, v, slots, tokens
 
     # -- read path -------------------------------------------------------------
 

@@ -141,6 +141,15 @@ struct DecodeArgs {
   int32_t* st;
   const int32_t* rows;   // q / out row of each listed sequence (NULL: row == sequence index)
   const int64_t* p_dev;  // pages listed, read on the device (NULL: total_pages)
+  // Fused KV-append (knew NULL: none). Row r's new token (knew/vnew[r], [n_kv][64])
+  // is written to its pool slot slots[r] and patched into the staged copy of the
+  // sequence's last page, where it must be the last written position.
+  const void* knew;
+  const void* vnew;
+  const int32_t* slots;
+  char* k_slab;          // this layer's K / V slab (slot * row_bytes addresses a row)
+  char* v_slab;
+  int64_t n_slots;
   int64_t total_pages;   // capacity of desc (and the page count when p_dev is NULL)
   int n_seqs;
   int n_rows;            // rows of q / out
@@ -342,7 +351,9 @@ __device__ __forceinline__ void attend_pages(const uint32_t (&kb)[U], const uint
 // online-softmax update. A piece cut by a range boundary is written as a
 // partial (O/l, m, l) per consumer warp and counted in with one atomic per
 // (sequence, KV head); the warp that completes a count merges those heads.
-template <typename T, int GROUPS, int NST, int MINB>
+// FUSE: the variant with the KV-append folded in (DecodeArgs::knew set); a
+// separate instantiation, so the plain decode kernel carries none of its code.
+template <typename T, int GROUPS, int NST, bool FUSE>
 __global__ void __maxnreg__(DK_MAXNREG) decode_kernel(const __grid_constant__ CUtensorMap tmap,
                                                       const DecodeArgs a) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -439,6 +450,35 @@ __global__ void __maxnreg__(DK_MAXNREG) decode_kernel(const __grid_constant__ CU
       slide_to(i);
       const int4 d = desc_at(i);
       const int st = i % NST;
+      if constexpr (FUSE) {
+        // Fused KV-append: before the TMA of a sequence's last page, the warp
+        // writes the sequence's new K/V row (all heads) to its slot and fences
+        // the stores for the async proxy, so the page lands with the token in
+        // place. The slot must be the page's last written position.
+        const int seq = d.y >> 7;
+        if (((d.y >> 5) & 1) && seq >= 0 && seq < a.n_seqs) {
+          const int row = a.rows ? __ldg(a.rows + seq) : seq;
+          if (row >= 0 && row < a.n_rows) {
+            const int slot = __ldg(a.slots + row);
+            const bool in_pool = slot >= 0 && slot < a.n_slots;
+            if (lane == 0 && slot != d.x * DK_P + (d.y & 31) - 1)
+              flag(a.st, in_pool ? PKV_DEV_META_BAD : PKV_DEV_SLOT_OOB);
+            if (in_pool) {
+              const int64_t rb = int64_t(n_cons) * DK_D * sizeof(T);  // one token row, all heads
+              const uint4* ks = reinterpret_cast<const uint4*>(static_cast<const char*>(a.knew) + row * rb);
+              const uint4* vs = reinterpret_cast<const uint4*>(static_cast<const char*>(a.vnew) + row * rb);
+              uint4* kd = reinterpret_cast<uint4*>(a.k_slab + slot * rb);
+              uint4* vd = reinterpret_cast<uint4*>(a.v_slab + slot * rb);
+              for (int e = lane; e < int(rb / 16); e += 32) {
+                kd[e] = __ldg(ks + e);
+                vd[e] = __ldg(vs + e);
+              }
+              asm volatile("fence.proxy.async.global;" ::: "memory");
+            }
+          }
+          __syncwarp();
+        }
+      }
       if (lane == 0 && !dead) {
         if (i >= NST && !mbar_wait_bounded_sleepy(&empty[st], ((i / NST) - 1) & 1, a.st, DK_PRODUCER_SLEEP_NS))
           dead = true;
@@ -521,7 +561,6 @@ __global__ void __maxnreg__(DK_MAXNREG) decode_kernel(const __grid_constant__ CU
 #pragma unroll
       for (int e = 0; e < 4; ++e) o[mt][e] = 0.f;
     float m0 = -1e30f, m1 = -1e30f, l0 = 0.f, l1 = 0.f;
-
     for (int j = 0; j < n; j += DK_U) {
       const int cnt = min(DK_U, n - j);
       slide_to(i + j);
@@ -548,8 +587,9 @@ __global__ void __maxnreg__(DK_MAXNREG) decode_kernel(const __grid_constant__ CU
                              v_chk, g);
         }
       }
+      // the next TMA into these stages lands after this warp's own stores to them
+      if (valid < DK_P) fence_proxy_async_smem();
       __syncwarp();
-      if (valid < DK_P && lane == 0) fence_proxy_async_smem();  // next TMA lands after the zero stores
       for (int u = 0; u < cnt; ++u) release(i + j + u);
     }
     i += n;
@@ -860,7 +900,7 @@ int decode_ctas_per_sm_cap() {
 
 // CTAs of the decode kernel resident per SM, cached per (device, n_kv_heads);
 // also raises the kernel's dynamic shared-memory limit on first use per device.
-template <typename T, int GROUPS, int NST, int MINB>
+template <typename T, int GROUPS, int NST, bool FUSE>
 int decode_grid_limit(int n_kv_heads) {
   static std::mutex mu;
   static std::vector<std::array<int, 9>> occ;
@@ -870,7 +910,7 @@ int decode_grid_limit(int n_kv_heads) {
   if ((int)occ.size() <= dev) occ.resize(dev + 1, std::array<int, 9>{});
   int& o = occ[dev][n_kv_heads];
   if (!o) {
-    auto fn = decode_kernel<T, GROUPS, NST, MINB>;
+    auto fn = decode_kernel<T, GROUPS, NST, FUSE>;
     const size_t sm = decode_smem(n_kv_heads, GROUPS, NST);
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm));
     int v = 0;
@@ -887,16 +927,22 @@ int decode_grid_limit(int n_kv_heads) {
 
 int max_decode_grid() { return num_sms() * 8; }
 
-template <typename T, int GROUPS, int NST, int MINB>
-int launch_decode_t(const pkv_pool& p, const CUtensorMap& tm, DecodeArgs& a, int64_t total_pages,
+template <typename T, int GROUPS, int NST, bool FUSE>
+int launch_decode_f(const pkv_pool& p, const CUtensorMap& tm, DecodeArgs& a, int64_t total_pages,
                     cudaStream_t s) {
-  int limit = decode_grid_limit<T, GROUPS, NST, MINB>(p.n_kv_heads);
+  int limit = decode_grid_limit<T, GROUPS, NST, FUSE>(p.n_kv_heads);
   if (limit <= 0) return PKV_ERR_CUDA;  // message already set
   limit = std::min(limit, max_decode_grid());
   const int grid = int(std::max<int64_t>(1, std::min<int64_t>(limit, total_pages)));
-  PKV_CUDA_RET(launch_kernel(decode_kernel<T, GROUPS, NST, MINB>, dim3(grid), dim3(32 * (p.n_kv_heads + 1)),
+  PKV_CUDA_RET(launch_kernel(decode_kernel<T, GROUPS, NST, FUSE>, dim3(grid), dim3(32 * (p.n_kv_heads + 1)),
                              decode_smem(p.n_kv_heads, GROUPS, NST), s, true, tm, a));
   return PKV_OK;
+}
+
+template <typename T, int GROUPS, int NST, int UNUSED>
+int launch_decode_t(const pkv_pool& p, const CUtensorMap& tm, DecodeArgs& a, int64_t tp, cudaStream_t s) {
+  return a.knew ? launch_decode_f<T, GROUPS, NST, true>(p, tm, a, tp, s)
+                : launch_decode_f<T, GROUPS, NST, false>(p, tm, a, tp, s);
 }
 
 template <typename T, int GROUPS>
@@ -1028,6 +1074,10 @@ extern "C" int pkv_attend_planned(const pkv_pool* pool, int32_t layer, int32_t n
     a.st = batch->dev_status;
     a.rows = nullptr;
     a.p_dev = nullptr;
+    a.knew = a.vnew = nullptr;
+    a.slots = nullptr;
+    a.k_slab = a.v_slab = nullptr;
+    a.n_slots = 0;
     a.total_pages = batch->total_pages;
     a.n_seqs = batch->n_seqs;
     a.n_rows = batch->n_tokens;
@@ -1061,6 +1111,10 @@ extern "C" int pkv_attend_planned(const pkv_pool* pool, int32_t layer, int32_t n
       a.st = batch->dev_status;
       a.rows = reinterpret_cast<const int32_t*>(ws + w.rows);
       a.p_dev = reinterpret_cast<const int64_t*>(ws + w.p_dec);
+      a.knew = a.vnew = nullptr;
+      a.slots = nullptr;
+      a.k_slab = a.v_slab = nullptr;
+      a.n_slots = 0;
       a.total_pages = batch->total_pages;
       a.n_seqs = batch->n_seqs;
       a.n_rows = batch->n_tokens;
@@ -1121,6 +1175,66 @@ extern "C" int pkv_attend_kernel(const pkv_pool* pool, int32_t n_heads, int32_t 
   return PKV_KERNEL_GENERIC;
 }
 
+extern "C" int pkv_append_attend_planned(const pkv_pool* pool, int32_t layer, int32_t n_heads, const void* k,
+                                         const void* v, const int32_t* slot_mapping, const void* q, void* out,
+                                         float scale, const pkv_batch* batch, int32_t decode_hint, void* workspace,
+                                         size_t workspace_bytes, void* stream) {
+  if (int rc = check_pool(pool)) return rc;
+  const pkv_pool& p = *pool;
+  if (layer < 0 || layer >= p.num_layers)
+    return fail(PKV_ERR_ARG, "layer_idx " + std::to_string(layer) + " out of range [0, " +
+                                 std::to_string(p.num_layers) + ")");
+  if (int rc = check_batch(p, n_heads, batch)) return rc;
+  if (!k || !v || !slot_mapping) return fail(PKV_ERR_ARG, "k, v and slot_mapping must be non-NULL");
+  if (!q || !out) return fail(PKV_ERR_ARG, "q and out must be non-NULL");
+  if (batch->n_tokens == 0) return PKV_OK;
+  const bool fused = decode_hint == 1 && decode_supported(p, n_heads) && batch->n_tokens == batch->n_seqs &&
+                     batch->total_pages > 0 &&
+                     ((reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v)) & 15) == 0;
+  if (!fused) {  // the two calls the fused launch replaces
+    if (int rc = pkv_append_kv(pool, layer, k, v, slot_mapping, batch->n_tokens, batch->dev_status, stream))
+      return rc;
+    return pkv_attend_planned(pool, layer, n_heads, q, out, scale, batch, decode_hint, workspace,
+                              workspace_bytes, stream);
+  }
+  const WsLayout w = step_layout(pool, n_heads, batch->n_seqs, batch->total_pages, true);
+  if (!workspace || workspace_bytes < w.total)
+    return fail(PKV_ERR_ARG, "workspace too small: need " + std::to_string(w.total) + " bytes");
+  if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(out)) & 15)
+    return fail(PKV_ERR_ARG, "q and out must be 16-byte aligned");
+  CUtensorMap tm;
+  if (int rc = get_tmap(p, &tm, p.n_kv_heads)) return rc;
+  char* ws = static_cast<char*>(workspace);
+  const int64_t sb = slab_bytes(p);
+  DecodeArgs a;
+  a.q = q;
+  a.out = out;
+  a.kv_indptr = batch->kv_indptr;
+  a.desc = reinterpret_cast<const int4*>(ws + w.page_desc);
+  a.partial_o = reinterpret_cast<float*>(ws + w.partial_o);
+  a.partial_ml = reinterpret_cast<float2*>(ws + w.partial_ml);
+  a.counters = reinterpret_cast<int32_t*>(ws + w.counters);
+  a.st = batch->dev_status;
+  a.rows = nullptr;
+  a.p_dev = nullptr;
+  a.knew = k;
+  a.vnew = v;
+  a.slots = slot_mapping;
+  a.k_slab = static_cast<char*>(p.base) + (2 * int64_t(layer)) * sb;
+  a.v_slab = a.k_slab + sb;
+  a.n_slots = p.num_blocks * p.block_size;
+  a.total_pages = batch->total_pages;
+  a.n_seqs = batch->n_seqs;
+  a.n_rows = batch->n_tokens;
+  a.n_heads = n_heads;
+  a.layer = layer;
+  a.scale_log2 = scale * 1.4426950408889634f;
+  const int groups = n_heads / p.n_kv_heads;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (p.dtype == PKV_F16) return launch_decode_g<__half>(p, groups, tm, a, batch->total_pages, s);
+  return launch_decode_g<__nv_bfloat16>(p, groups, tm, a, batch->total_pages, s);
+}
+
 extern "C" int pkv_attend(const pkv_pool* pool, int32_t layer, int32_t n_heads, const void* q,
                           void* out, float scale, const pkv_batch* batch, int32_t decode_hint,
                           void* workspace, size_t workspace_bytes, void* stream) {
@@ -1176,10 +1290,10 @@ int noalloc_scratch(void** out) {
 template <typename T, int GROUPS>
 int decode_grid_cap_n(const pkv_pool& p) {
   switch (decode_nst()) {
-    case 3: return decode_grid_limit<T, GROUPS, 3, 1>(p.n_kv_heads);
-    case 5: return decode_grid_limit<T, GROUPS, 5, 1>(p.n_kv_heads);
-    case 6: return decode_grid_limit<T, GROUPS, 6, 1>(p.n_kv_heads);
-    default: return decode_grid_limit<T, GROUPS, 4, 1>(p.n_kv_heads);
+    case 3: return decode_grid_limit<T, GROUPS, 3, false>(p.n_kv_heads);
+    case 5: return decode_grid_limit<T, GROUPS, 5, false>(p.n_kv_heads);
+    case 6: return decode_grid_limit<T, GROUPS, 6, false>(p.n_kv_heads);
+    default: return decode_grid_limit<T, GROUPS, 4, false>(p.n_kv_heads);
   }
 }
 template <typename T>
@@ -1250,6 +1364,10 @@ extern "C" int pkv_attend_decode_noalloc(const pkv_pool* pool, int32_t layer, in
   a.st = batch->dev_status;
   a.rows = nullptr;
   a.p_dev = nullptr;
+  a.knew = a.vnew = nullptr;
+  a.slots = nullptr;
+  a.k_slab = a.v_slab = nullptr;
+  a.n_slots = 0;
   a.total_pages = batch->total_pages;
   a.n_seqs = batch->n_seqs;
   a.n_rows = batch->n_tokens;

@@ -112,8 +112,11 @@ class RandomLlama:
             q = self._rope(qkv[:, : Hq * Dh].view(T, Hq, Dh), cos, sin)
             k = self._rope(qkv[:, Hq * Dh: (Hq + Hkv) * Dh].view(T, Hkv, Dh), cos, sin)
             v = qkv[:, (Hq + Hkv) * Dh:].reshape(T, Hkv, Dh)
-            backend.append_kv(layer, k, v, meta)
-            o = backend.attend(q, layer, self.scale, meta)
+            if hasattr(backend, "append_attend"):  # one call (one launch for a decode step)
+                o = backend.append_attend(layer, k, v, q, self.scale, meta)
+            else:
+                backend.append_kv(layer, k, v, meta)
+                o = backend.attend(q, layer, self.scale, meta)
             x = x + F.linear(o.reshape(T, Hq * Dh), self.w_o[layer])
             h = self._norm(x, self.ln_ffn[layer])
             gu = F.linear(h, self.w_gate_up[layer])
