@@ -69,6 +69,44 @@ def dist_env():
     return ws, rank, local
 
 
+# Cross-rank reductions of the replica bench (device = the rank's GPU, or the
+# CPU under gloo in the tests). Replicas exchange only these scalars.
+
+def max_over_ranks(dist, ms: float, device) -> float:
+    """The job's elapsed time: the slowest rank's."""
+    import torch
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size() == 1:
+        return ms
+    t = torch.tensor([ms], device=device, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(dist, vals: list[float], device) -> list[float]:
+    """Aggregate rates of independent replicas."""
+    import torch
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size() == 1:
+        return list(vals)
+    t = torch.tensor(vals, device=device, dtype=torch.float64)
+    dist.all_reduce(t)
+    return [float(x) for x in t.tolist()]
+
+
+def job_gpu_ids(dist, gpu_id: str) -> str:
+    """Every rank's GPU id, comma-joined in rank order (for nvidia-smi -i)."""
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size() == 1:
+        return gpu_id
+    ids = [None] * dist.get_world_size()
+    dist.all_gather_object(ids, gpu_id)
+    return ",".join(ids)
+
+
+def replica_value(n_seq: int, ws: int, steps: int, max_ms: float) -> float:
+    """Whole-job tok/s: every rank decodes n_seq tokens per step; the job's
+    time is the slowest rank's."""
+    return n_seq * ws * steps / (max_ms / 1e3)
+
+
 class ClockSampler:
     """nvidia-smi clocks / throttle reasons of the job's GPUs (comma-separated
     UUIDs), sampled every 20 ms while the timed region runs; start() returns
@@ -359,10 +397,7 @@ def run_b200(args) -> None:
         gpu_id = f"GPU-{uuid}" if not str(uuid).startswith("GPU-") else str(uuid)
     except Exception:
         pass
-    if ws > 1:
-        ids = [None] * ws
-        dist.all_gather_object(ids, gpu_id)
-        gpu_id = ",".join(ids)
+    gpu_id = job_gpu_ids(dist, gpu_id)
     clocks = ClockSampler(gpu_id)
     if rank == 0:
         clocks.start()
@@ -376,15 +411,12 @@ def run_b200(args) -> None:
     e1.record()
     torch.cuda.synchronize()
     clock_info = clocks.stop()
-    ms = e0.elapsed_time(e1)
+    ms = max_over_ranks(dist, e0.elapsed_time(e1), device)
     if ws > 1:
-        t = torch.tensor([ms], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
         dist.barrier()
-        ms = float(t.item())
     bk.check_status()
     ms_per_step = ms / args.steps
-    value = N_SEQ * ws * args.steps / (ms / 1e3)
+    value = replica_value(N_SEQ, ws, args.steps, ms)
 
     # ---- roofline of the decode kernel (its launches inside the graphs)
     # every timed step replays graph s % n_graphs once: weight each graph's
@@ -439,11 +471,7 @@ def run_b200(args) -> None:
             fgraphs[s % n_graphs].replay()
         e1.record()
         torch.cuda.synchronize()
-        fms = e0.elapsed_time(e1)
-        if ws > 1:
-            t = torch.tensor([fms], device=device)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            fms = float(t.item())
+        fms = max_over_ranks(dist, e0.elapsed_time(e1), device)
         bk.check_status()
         fl = [a.elapsed_time(b) / L for a, b in fev]
         falg = alg_bytes + N_SEQ * HKV * D * 2 * 2 * 2  # plus the new K/V rows read and written to their slots
@@ -471,10 +499,9 @@ def run_b200(args) -> None:
             dist.barrier()
         ll = run_llama(torch, bk, args, device, rank)
         if ws > 1:
-            t = torch.tensor([ll["generated_tok_per_s"], ll["processed_tok_per_s"]], device=device, dtype=torch.float64)
-            dist.all_reduce(t)
-            ll["aggregate_generated_tok_per_s"] = round(float(t[0]), 1)
-            ll["aggregate_processed_tok_per_s"] = round(float(t[1]), 1)
+            g, p_ = sum_over_ranks(dist, [ll["generated_tok_per_s"], ll["processed_tok_per_s"]], device)
+            ll["aggregate_generated_tok_per_s"] = round(g, 1)
+            ll["aggregate_processed_tok_per_s"] = round(p_, 1)
         line_extra["llama"] = ll
     if ws > 1:
         dist.barrier()
@@ -564,11 +591,7 @@ def run_e2e(torch, bk, tables, ctx, args, device, ws, dist, n_graphs) -> dict:
         one(s)
     e1.record()
     torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1)
-    if ws > 1:
-        t = torch.tensor([ms], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    ms = max_over_ranks(dist, e0.elapsed_time(e1), device)
     bk.check_status()
     h2d = L * (hq[0].numel() + hk[0].numel() + hv[0].numel()) * 2 + meta_bytes
     d2h = L * hout[0].numel() * 2

@@ -107,3 +107,33 @@ def test_batchmeta_validate_messages():
         dataclasses.replace(m, kv_lens=torch.tensor([999], dtype=torch.int32)).validate()
     with pytest.raises(AssertionError, match="batch_indices"):
         dataclasses.replace(m, batch_indices=torch.tensor([0, 0], dtype=torch.int32)).validate()
+
+
+def test_kernel_selection_for_batch_shapes(lib):
+    """pkv_attend_kernel is host-only: which kernel each batch shape and hint
+    takes (decode for pure decode, the tensor-core prefill kernel for
+    chunked / mixed batches, the generic kernel elsewhere)."""
+    import ctypes
+    buf = (ctypes.c_char * 64)()
+    base = (ctypes.addressof(buf) + 15) & ~15
+
+    def pool(dtype, n_kv=8, head_dim=64, block=16):
+        return N.PoolDesc(base, 64, 2, block, n_kv, head_dim, dtype, 0)
+
+    K = {0: "generic", 1: "decode", 2: "prefill"}
+    f16, f32 = 0, 2
+    cases = [
+        (pool(f16), 32, 256, 256, 1, "decode"),
+        (pool(f16), 32, 4, 700, 0, "prefill"),     # chunked prefill / mixed
+        (pool(f16), 32, 4, 700, 2, "prefill"),     # pure prefill
+        (pool(f16), 32, 3, 3, 0, "generic"),       # q_lens like [2, 0, 1]: n_tokens == n_seqs, not decode
+        (pool(f32), 32, 256, 256, 1, "generic"),   # fp32 pools: CUDA-core kernel
+        (pool(f16, head_dim=128), 32, 4, 700, 0, "generic"),
+        (pool(f16, n_kv=8), 24, 4, 700, 0, "generic"),  # 3 query heads per KV head
+        (pool(f16, n_kv=4), 32, 8, 8, 1, "decode"),     # 8 query heads per KV head
+        (pool(1), 32, 4, 700, 0, "prefill"),       # bf16
+    ]
+    for p, hq, n, t, hint, want in cases:
+        got = lib.pkv_attend_kernel(ctypes.byref(p), hq, n, t, hint)
+        assert K[got] == want, (p.dtype, p.head_dim, p.n_kv_heads, hq, n, t, hint, got)
+    assert lib.pkv_attend_kernel(ctypes.byref(pool(f16)), 30, 4, 700, 0) < 0  # 30 % 8 != 0
