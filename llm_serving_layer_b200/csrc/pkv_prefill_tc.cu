@@ -176,6 +176,8 @@ __global__ void __launch_bounds__(TC_THREADS, 2) prefill_tc_kernel(const __grid_
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tile_idx = int(blockIdx.x) / a.n_kv, h = int(blockIdx.x) % a.n_kv;
+  pdl_trigger();
+  pdl_wait();  // the plan, q and this step's append are written by earlier kernels
   if (tile_idx >= *a.n_tiles) return;
   const int2 tile = a.tiles[tile_idx];
   const int s = tile.x, j0 = tile.y;
@@ -485,8 +487,7 @@ int launch_tc_t(const pkv_pool& p, const CUtensorMap& tm, const TcArgs& a, int g
       ready[dev] = 1;
     }
   }
-  prefill_tc_kernel<T, G><<<grid, TC_THREADS, tc_smem(), s>>>(tm, a);
-  PKV_CUDA_RET(cudaGetLastError());
+  PKV_CUDA_RET(launch_kernel(prefill_tc_kernel<T, G>, dim3(grid), dim3(TC_THREADS), tc_smem(), s, true, tm, a));
   return PKV_OK;
 }
 
