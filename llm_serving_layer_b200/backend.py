@@ -100,6 +100,10 @@ class B200PagedBackend:
         )
         self._pdesc = ctypes.byref(self._desc)
         self._status = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self._status_ptr = self._status.data_ptr()
+        self._dev_index = self.device.index if self.device.index is not None else torch.cuda.current_device()
+        self._slots_meta: Any = None  # the meta whose int32 slot map is cached in _slots
+        self._slots: torch.Tensor | None = None
         self._ws: torch.Tensor | None = None
         # per-step state, keyed by BatchMeta identity (a strong reference keeps
         # the id from being recycled while it is cached)
@@ -180,8 +184,8 @@ class B200PagedBackend:
         if tokens == 0:
             return
         N.check(self._lib.pkv_append_kv(self._pdesc, layer_idx, k.data_ptr(), v.data_ptr(),
-                                        slots.data_ptr(), tokens, self._status.data_ptr(),
-                                        N.stream_ptr(self.device)), "append_kv")
+                                        slots.data_ptr(), tokens, self._status_ptr,
+                                        torch.cuda.current_stream(self.device).cuda_stream), "append_kv")
 
     def append_attend(self, layer_idx: int, k: torch.Tensor, v: torch.Tensor, q: torch.Tensor,
                       scale: float, meta: Any) -> torch.Tensor:
@@ -198,7 +202,7 @@ class B200PagedBackend:
         st = self._step_state(meta)
         if st["n_tokens"] != tokens:
             raise ValueError(f"meta describes {st['n_tokens']} tokens but q has {tokens}")
-        q = q.to(device=self.device, dtype=self.dtype).contiguous()
+        q = self._own(q, self.dtype)
         out = torch.empty_like(q)
         if tokens == 0:
             return out
@@ -206,8 +210,8 @@ class B200PagedBackend:
         self.last_kernel = st["kernel"]
         N.check(self._lib.pkv_append_attend_planned(
             self._pdesc, layer_idx, self.n_heads, k.data_ptr(), v.data_ptr(), slots.data_ptr(), q.data_ptr(),
-            out.data_ptr(), float(scale), ctypes.byref(st["batch"]), st["hint"], st["ws_ptr"], st["ws_bytes"],
-            N.stream_ptr(self.device)), "append_attend")
+            out.data_ptr(), float(scale), st["batch_ref"], st["hint"], st["ws_ptr"], st["ws_bytes"],
+            torch.cuda.current_stream(self.device).cuda_stream), "append_attend")
         return out
 
     def _append_args(self, layer_idx: int, k: torch.Tensor, v: torch.Tensor, meta: Any):
@@ -228,10 +232,14 @@ class B200PagedBackend:
             raise ValueError(
                 f"slot_mapping has {meta.slot_mapping.shape[0]} entries but {tokens} tokens were supplied"
             )
-        k = k.to(device=self.device, dtype=self.dtype).contiguous()
-        v = v.to(device=self.device, dtype=self.dtype).contiguous()
-        slots = self._i32(meta.slot_mapping) if tokens else None
-        return k, v, slots, tokens
+        k = self._own(k, self.dtype)
+        v = self._own(v, self.dtype)
+        if not tokens:
+            return k, v, None, tokens
+        if self._slots_meta is not meta:  # the int32 device slot map, once per meta
+            self._slots = self._i32(meta.slot_mapping)
+            self._slots_meta = meta
+        return k, v, self._slots, tokens
 
     # -- read path -------------------------------------------------------------
 
@@ -249,7 +257,7 @@ class B200PagedBackend:
         st = self._step_state(meta)
         if st["n_tokens"] != tokens:
             raise ValueError(f"meta describes {st['n_tokens']} tokens but q has {tokens}")
-        q = q.to(device=self.device, dtype=self.dtype).contiguous()
+        q = self._own(q, self.dtype)
         out = torch.empty_like(q)
         if tokens == 0:
             return out
@@ -257,8 +265,8 @@ class B200PagedBackend:
         self.last_kernel = st["kernel"]
         N.check(self._lib.pkv_attend_planned(
             self._pdesc, layer_idx, self.n_heads, q.data_ptr(), out.data_ptr(), float(scale),
-            ctypes.byref(st["batch"]), st["hint"], st["ws_ptr"], st["ws_bytes"],
-            N.stream_ptr(self.device)), "attend")
+            st["batch_ref"], st["hint"], st["ws_ptr"], st["ws_bytes"],
+            torch.cuda.current_stream(self.device).cuda_stream), "attend")
         return out
 
     # -- per-step plan -----------------------------------------------------------
@@ -325,7 +333,8 @@ class B200PagedBackend:
                                        N.stream_ptr(self.device)), "plan")
             self.n_plans += 1
         self._meta = meta
-        self._meta_state = {"batch": batch, "tensors": t, "decode": decode, "hint": hint, "n_tokens": n_tokens,
+        self._meta_state = {"batch": batch, "batch_ref": ctypes.byref(batch), "tensors": t, "decode": decode,
+                            "hint": hint, "n_tokens": n_tokens,
                             "ws_ptr": ws_ptr, "ws_bytes": ws_bytes, "kernel": N.KERNEL_NAMES[kernel]}
         return self._meta_state
 
@@ -377,6 +386,8 @@ class B200PagedBackend:
         BatchMeta's tensors in place and reuses the object)."""
         self._meta = None
         self._meta_state = {}
+        self._slots_meta = None
+        self._slots = None
 
     # -- status -----------------------------------------------------------------
 
@@ -393,6 +404,12 @@ class B200PagedBackend:
 
     def _i32(self, t: torch.Tensor) -> torch.Tensor:
         return t.to(device=self.device, dtype=torch.int32).contiguous()
+
+    def _own(self, t: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+        """t on this device in `dtype`, contiguous (no op when it already is)."""
+        if t.is_cuda and t.dtype == dtype and t.get_device() == self._dev_index and t.is_contiguous():
+            return t
+        return t.to(device=self.device, dtype=dtype).contiguous()
 
     def _check_layer(self, layer_idx: int) -> None:
         if layer_idx is None or not 0 <= layer_idx < self.num_layers:
