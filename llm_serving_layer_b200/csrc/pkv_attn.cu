@@ -34,7 +34,7 @@ namespace {
 
 constexpr int DK_D = 64;       // head_dim of the decode kernel
 constexpr int DK_P = 16;       // tokens per page of the decode kernel
-constexpr int DK_NST = 4;                  // default ring depth (pages in flight per CTA)
+constexpr int DK_NST = 6;                  // default ring depth (pages in flight per CTA)
 constexpr int DK_KV_MAX = 8;               // KV heads of the decode kernel (one consumer warp each)
 constexpr int DK_WMERGE = 4;               // split-K pieces fetched per round of loads in a merge
 constexpr int DK_U = 2;                    // pages folded per online-softmax update
