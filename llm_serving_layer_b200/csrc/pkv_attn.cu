@@ -38,9 +38,6 @@ constexpr int DK_NST = 6;                  // default ring depth (pages in fligh
 constexpr int DK_KV_MAX = 8;               // KV heads of the decode kernel (one consumer warp each)
 constexpr int DK_WMERGE = 4;               // split-K pieces fetched per round of loads in a merge
 constexpr int DK_U = 2;                    // pages folded per online-softmax update
-#ifndef DK_TAIL_FIRST
-#define DK_TAIL_FIRST 0                    // process the range's tail piece first
-#endif
 #ifndef DK_PRODUCER_SLEEP_NS
 #define DK_PRODUCER_SLEEP_NS 64            // producer back-off while the ring is full
 #endif
@@ -133,7 +130,6 @@ __global__ void plan_kernel(const int32_t* __restrict__ kv_indptr,
 struct DecodeArgs {
   const void* q;
   void* out;
-  const int32_t* kv_indptr;
   const int4* desc;
   float* partial_o;    // [2 * grid][n_heads][D]   O / l of each split piece
   float2* partial_ml;  // [2 * grid][n_heads]      (m, l) of each split piece
@@ -392,33 +388,12 @@ __global__ void __maxnreg__(DK_MAXNREG) decode_kernel(const __grid_constant__ CU
   }
   __syncthreads();
 
-  // Processing order. The range's last sequence (tail piece T) and first
-  // sequence (head piece H) may be cut by the range's ends; T is taken first,
-  // then H, then the middle M, so that split pieces are published early and
-  // their merges overlap the consumers' remaining work.
-  const int4 dfirst = a.desc[p0], dlast = a.desc[p1 - 1];
-  int lenT = 0, lenH = 0;
-  int64_t hend = p0, tstart = p1;
-  {
-    const int sf = dfirst.y >> 7, sl = dlast.y >> 7;
-    if (DK_TAIL_FIRST && sf >= 0 && sl >= 0 && sf != sl && dfirst.w > p0 && dfirst.w <= p1 &&
-        dlast.z >= p0 && dlast.z < p1) {
-      hend = dfirst.w;
-      tstart = dlast.z;
-      lenT = int(p1 - tstart);
-      lenH = int(hend - p0);
-    }
-  }
-  auto pos = [&](int i) -> int64_t {  // processing step -> page index
-    if (i < lenT) return tstart + i;
-    if (i < lenT + lenH) return p0 + (i - lenT);
-    return (lenT ? hend : p0) + (i - lenT - lenH);
-  };
-  auto seg_end = [&](int i) -> int64_t {  // one past the last page of step i's segment
-    if (i < lenT) return p1;
-    if (i < lenT + lenH) return hend;
-    return lenT ? tstart : p1;
-  };
+  // The range is processed in page order: its first sequence (possibly cut at
+  // p0, its piece published for the merge), the sequences inside it, its last
+  // (possibly cut at p1).
+  const int4 dfirst = a.desc[p0];
+  auto pos = [&](int i) -> int64_t { return p0 + i; };  // processing step -> page index
+  auto seg_end = [&](int i) -> int64_t { return p1; };  // one past the range's last page
   // page descriptors: lane j holds window entries [wb + j] (cur) and [wb + 32 + j] (nxt)
   int wb = 0;
   int4 dcur = make_int4(-1, -1, -1, -1), dnxt = make_int4(-1, -1, -1, -1);
@@ -551,7 +526,7 @@ __global__ void __maxnreg__(DK_MAXNREG) decode_kernel(const __grid_constant__ CU
       load_q_frag<T, GROUPS>(q, row, a.n_heads, h, g, c4, qb);
     }
     // the sequence processed next: H's after T, then each M in turn
-    nxt_seq = (i < lenT) ? (dfirst.y >> 7) : seq + 1;
+    nxt_seq = seq + 1;
     nxt_row = (nxt_seq >= 0 && nxt_seq < a.n_seqs) ? row_of(nxt_seq) : -1;
     if (nxt_row >= 0 && nxt_row < a.n_rows) load_q_frag<T, GROUPS>(q, nxt_row, a.n_heads, h, g, c4, qn);
     else nxt_seq = -1;
@@ -1066,7 +1041,6 @@ extern "C" int pkv_attend_planned(const pkv_pool* pool, int32_t layer, int32_t n
     DecodeArgs a;
     a.q = q;
     a.out = out;
-    a.kv_indptr = batch->kv_indptr;
     a.desc = reinterpret_cast<const int4*>(ws + w.page_desc);
     a.partial_o = reinterpret_cast<float*>(ws + w.partial_o);
     a.partial_ml = reinterpret_cast<float2*>(ws + w.partial_ml);
@@ -1103,8 +1077,7 @@ extern "C" int pkv_attend_planned(const pkv_pool* pool, int32_t layer, int32_t n
       DecodeArgs a;
       a.q = q;
       a.out = out;
-      a.kv_indptr = batch->kv_indptr;
-      a.desc = reinterpret_cast<const int4*>(ws + w.page_desc);
+        a.desc = reinterpret_cast<const int4*>(ws + w.page_desc);
       a.partial_o = reinterpret_cast<float*>(ws + w.partial_o);
       a.partial_ml = reinterpret_cast<float2*>(ws + w.partial_ml);
       a.counters = reinterpret_cast<int32_t*>(ws + w.counters);
@@ -1209,7 +1182,6 @@ extern "C" int pkv_append_attend_planned(const pkv_pool* pool, int32_t layer, in
   DecodeArgs a;
   a.q = q;
   a.out = out;
-  a.kv_indptr = batch->kv_indptr;
   a.desc = reinterpret_cast<const int4*>(ws + w.page_desc);
   a.partial_o = reinterpret_cast<float*>(ws + w.partial_o);
   a.partial_ml = reinterpret_cast<float2*>(ws + w.partial_ml);
@@ -1356,7 +1328,6 @@ extern "C" int pkv_attend_decode_noalloc(const pkv_pool* pool, int32_t layer, in
   DecodeArgs a;
   a.q = q;
   a.out = out;
-  a.kv_indptr = batch->kv_indptr;
   a.desc = reinterpret_cast<const int4*>(ws + w.page_desc);
   a.partial_o = reinterpret_cast<float*>(ws + w.partial_o);
   a.partial_ml = reinterpret_cast<float2*>(ws + w.partial_ml);
