@@ -484,7 +484,9 @@ def run_b200(args) -> None:
         del fgraphs
 
     # ---- e2e: public API, host buffers, H2D + D2H inside the timed region
-    e2e = run_e2e(torch, bk, tables, ctx, args, device, ws, dist, n_graphs)
+    e2e = run_e2e(torch, bk, tables, ctx, args, device, ws, dist, n_graphs, "device")
+    host_e2e = run_e2e(torch, bk, tables, ctx, args, device, ws, dist, n_graphs, "host")
+    e2e["host_meta"] = {k: host_e2e[k] for k in ("value", "ms_per_step", "h2d_bytes_per_step", "path")}
 
     line_extra = {}
     # ---- swap (config 4), rank 0 measures its own GPU's host link
@@ -544,40 +546,56 @@ def run_b200(args) -> None:
         dist.destroy_process_group()
 
 
-def run_e2e(torch, bk, tables, ctx, args, device, ws, dist, n_graphs) -> dict:
-    """Public-API end to end: per step, build the BatchMeta on the host, copy it
-    and the step's q/k/v (16 layers) from pinned host memory, run append_kv +
-    attend per layer (the reference engine's calls), copy every layer's
-    attention output back to pinned host memory, synchronise. The copies run on
-    a side stream, ordered by events: layer l waits only for its own inputs,
-    and its output leaves as soon as layer l finished. Timed with CUDA events
-    around the whole loop."""
+def run_e2e(torch, bk, tables, ctx, args, device, ws, dist, n_graphs, meta_mode="device") -> dict:
+    """Public-API end to end: per step, the step's BatchMeta (``meta_mode``
+    "device": DeviceBlockTables.build_batch_meta, the rows' lengths plus the
+    blocks of rows that crossed into a new page copied in one pinned transfer
+    and every field computed on the GPU; "host": build_meta on the host and one
+    copy per field), the step's q/k/v for 16 layers copied from pinned host
+    memory (one buffer per layer), append_kv + attend per layer (the reference
+    engine's calls), every layer's attention output copied back to pinned host
+    memory, one synchronize. The copies run on a side stream, ordered by
+    events: layer l waits only for its own inputs, and its output leaves as
+    soon as layer l finished; the next step's meta is built on the host while
+    this step's GPU work runs. Timed with CUDA events around the whole loop."""
+    from llm_serving_layer_b200 import DeviceBlockTables
     from llm_serving_layer_b200.meta import build_meta
 
     steps = args.e2e_steps
     base = args.warmup  # fresh lengths continue from the graph steps' start
     rs = np.random.RandomState(args.seed + 7)
-    hq = [torch.from_numpy(rs.standard_normal((N_SEQ, HQ, D)).astype(np.float16)).pin_memory() for _ in range(L)]
-    hk = [torch.from_numpy((rs.standard_normal((N_SEQ, HKV, D)) * KV_STD).astype(np.float16)).pin_memory()
-          for _ in range(L)]
-    hv = [torch.from_numpy((rs.standard_normal((N_SEQ, HKV, D)) * KV_STD).astype(np.float16)).pin_memory()
-          for _ in range(L)]
+    nq, nk = N_SEQ * HQ * D, N_SEQ * HKV * D
+    hx = []
+    for _ in range(L):  # one pinned buffer per layer: q | k | v
+        x = np.concatenate([rs.standard_normal(nq), rs.standard_normal(2 * nk) * KV_STD]).astype(np.float16)
+        hx.append(torch.from_numpy(x).pin_memory())
     hout = [torch.empty((N_SEQ, HQ, D), dtype=torch.float16).pin_memory() for _ in range(L)]
-    dq = [torch.empty_like(x, device=device) for x in hq]
-    dk = [torch.empty_like(x, device=device) for x in hk]
-    dv = [torch.empty_like(x, device=device) for x in hv]
-    meta_bytes = 0
+    dx = [torch.empty_like(x, device=device) for x in hx]
+    dq = [x[:nq].view(N_SEQ, HQ, D) for x in dx]
+    dk = [x[nq:nq + nk].view(N_SEQ, HKV, D) for x in dx]
+    dv = [x[nq + nk:].view(N_SEQ, HKV, D) for x in dx]
     comp = torch.cuda.current_stream(device)
     cstream = torch.cuda.Stream(device=device)
     ev_in = [torch.cuda.Event() for _ in range(L)]
     ev_out = [torch.cuda.Event() for _ in range(L)]
+    rows = np.arange(N_SEQ, dtype=np.int32)
+    ones = np.ones(N_SEQ, dtype=np.int64)
+    max_pages = max(len(t) for t in tables)
+    bt = DeviceBlockTables(N_SEQ, max_pages, P, bk.num_blocks, device=device, ring=3, status=bk._status)
+    meta_in = {"bytes": 0, "n": 0}
 
     def meta_for_step(s):
-        nonlocal meta_bytes
-        m = build_meta(tables, ctx + base + (s % n_graphs), [1] * N_SEQ, P, device=device, pin=True)
-        meta_bytes = sum(int(getattr(m, f).numel() * getattr(m, f).element_size()) for f in (
-            "query_lens", "cu_query_lens", "kv_lens", "positions", "last_token_ix", "kv_indptr",
-            "kv_indices", "kv_last_page_len", "batch_indices", "slot_mapping"))
+        kv = ctx + base + (s % n_graphs)
+        if meta_mode == "host":
+            m = build_meta(tables, kv, ones, P, device=device, pin=True)
+            meta_in["bytes"] += sum(int(getattr(m, f).numel() * getattr(m, f).element_size()) for f in (
+                "query_lens", "cu_query_lens", "kv_lens", "positions", "last_token_ix", "kv_indptr",
+                "kv_indices", "kv_last_page_len", "batch_indices", "slot_mapping"))
+        else:
+            nu = bt.extend_to(rows, kv, tables)  # blocks of rows that crossed into a new page
+            m = bt.build_batch_meta(rows, ones, kv)
+            meta_in["bytes"] += 4 * (3 * N_SEQ + 3 * nu)
+        meta_in["n"] += 1
         return m
 
     nxt = {}
@@ -589,9 +607,7 @@ def run_e2e(torch, bk, tables, ctx, args, device, ws, dist, n_graphs) -> dict:
         cstream.wait_stream(comp)  # the previous step is done with the device buffers
         with torch.cuda.stream(cstream):
             for layer in range(L):
-                dq[layer].copy_(hq[layer], non_blocking=True)
-                dk[layer].copy_(hk[layer], non_blocking=True)
-                dv[layer].copy_(hv[layer], non_blocking=True)
+                dx[layer].copy_(hx[layer], non_blocking=True)
                 ev_in[layer].record(cstream)
         outs = []
         for layer in range(L):
@@ -605,10 +621,14 @@ def run_e2e(torch, bk, tables, ctx, args, device, ws, dist, n_graphs) -> dict:
         nxt[s + 1] = meta_for_step(s + 1)
         cstream.synchronize()
 
+    if meta_mode == "device":  # admission: each row gets the blocks of its history
+        for r in range(N_SEQ):
+            bt.bind(r, tables[r][:(int(ctx[r]) + base + P - 1) // P])
     for s in range(3):
         one(s)
     nxt.clear()
     nxt[0] = meta_for_step(0)
+    meta_in.update(bytes=0, n=0)
     if ws > 1:
         dist.barrier()
     torch.cuda.synchronize()
@@ -620,12 +640,15 @@ def run_e2e(torch, bk, tables, ctx, args, device, ws, dist, n_graphs) -> dict:
     torch.cuda.synchronize()
     ms = max_over_ranks(dist, e0.elapsed_time(e1), device)
     bk.check_status()
-    h2d = L * (hq[0].numel() + hk[0].numel() + hv[0].numel()) * 2 + meta_bytes
+    h2d = L * hx[0].numel() * 2 + meta_in["bytes"] // max(meta_in["n"], 1)
     d2h = L * hout[0].numel() * 2
+    path = ("B200PagedBackend.append_kv/attend per layer, validate='device', "
+            + ("DeviceBlockTables.build_batch_meta (BatchMeta fields computed on the GPU from device block "
+               "tables; only new blocks travel)" if meta_mode == "device" else
+               "host build_meta (one copy per BatchMeta field)")
+            + " built per step (the next step's while this one runs), copies on a side stream")
     return {"value": round(N_SEQ * ws * steps / (ms / 1e3), 1), "unit": UNIT, "h2d_bytes_per_step": int(h2d),
-            "d2h_bytes_per_step": int(d2h), "steps": steps, "ms_per_step": round(ms / steps, 4),
-            "path": ("B200PagedBackend.append_kv/attend per layer, validate='device', host BatchMeta built "
-                     "per step (the next step's while this one runs), copies on a side stream")}
+            "d2h_bytes_per_step": int(d2h), "steps": steps, "ms_per_step": round(ms / steps, 4), "path": path}
 
 
 def prefill_workload(seed: int):
@@ -1003,11 +1026,13 @@ def run_llama(torch, bk, args, device, rank) -> dict:
     every running sequence past its prompt and prefills at most 512 prompt
     tokens (the reference scheduler's max_prefill_tokens); a waiting request is
     admitted when a slot is free and prefill budget is left. Greedy sampling on
-    the GPU, one host readback of the step's tokens. Wall clock per step: host
-    batch assembly (build_meta), H2D of the metadata and tokens, the 16-layer
-    forward, D2H of the tokens."""
+    the GPU, one host readback of the step's tokens. Each running sequence owns
+    a row of DeviceBlockTables (blocks recorded as they are allocated; the
+    step's BatchMeta computed on the GPU). Wall clock per step: host scheduling
+    and batch assembly, H2D of the step's rows / lengths / new blocks and
+    tokens, the 16-layer forward, D2H of the tokens."""
+    from llm_serving_layer_b200 import DeviceBlockTables
     from llm_serving_layer_b200.llama import LlamaConfig, RandomLlama
-    from llm_serving_layer_b200.meta import build_meta
 
     cfg = LlamaConfig()
     model = RandomLlama(cfg, device, seed=args.seed + 17)
@@ -1015,8 +1040,12 @@ def run_llama(torch, bk, args, device, rank) -> dict:
     n_run, budget, lam = 1024, 512, 6.0
 
     free = list(rs.permutation(bk.num_blocks))
+    bt = DeviceBlockTables(n_run, (2048 + P - 1) // P + 1, P, bk.num_blocks, device=device,
+                           max_tokens=n_run + budget, status=bk._status)
+    free_rows = list(range(n_run))
+
     class S:
-        __slots__ = ("blocks", "n", "prompt", "pos", "target", "last")
+        __slots__ = ("blocks", "n", "prompt", "pos", "target", "last", "row")
     running, queue = [], []
 
     def new_req():
@@ -1037,6 +1066,8 @@ def run_llama(torch, bk, args, device, rank) -> dict:
         r.blocks = [int(free.pop()) for _ in range(nb)]
         hist_blocks += r.blocks
         r.last = int(rs.randint(0, cfg.vocab))
+        r.row = free_rows.pop()
+        bt.bind(r.row, r.blocks)
         running.append(r)
     idx = torch.tensor(hist_blocks, device=device, dtype=torch.int64)
     g = torch.Generator(device=device).manual_seed(args.seed + 19)
@@ -1053,6 +1084,7 @@ def run_llama(torch, bk, args, device, rank) -> dict:
         while len(running) < n_run and queue and pending < budget:
             r = queue.pop(0)
             pending += len(r.prompt)
+            r.row = free_rows.pop()
             running.append(r)
         left = budget
         batch, qtok = [], []
@@ -1069,11 +1101,12 @@ def run_llama(torch, bk, args, device, rank) -> dict:
                 qtok.append(np.asarray([r.last]))
         for r, q in batch:
             need = (r.n + q + P - 1) // P - len(r.blocks)
-            for _ in range(need):
-                r.blocks.append(int(free.pop()))
+            if need > 0:
+                new = [int(free.pop()) for _ in range(need)]
+                r.blocks += new
+                bt.extend(r.row, new)
             r.n += q
-        meta = build_meta([r.blocks for r, _ in batch], [r.n for r, _ in batch], [q for _, q in batch], P,
-                          device=device)
+        meta = bt.build_batch_meta([r.row for r, _ in batch], [q for _, q in batch], [r.n for r, _ in batch])
         toks = torch.from_numpy(np.concatenate(qtok).astype(np.int64)).pin_memory().to(device, non_blocking=True)
         ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
         ev[0].record()
@@ -1096,6 +1129,8 @@ def run_llama(torch, bk, args, device, rank) -> dict:
         for r in done:
             running.remove(r)
             free.extend(r.blocks)
+            bt.release(r.row)
+            free_rows.append(r.row)
         for _ in range(rs.poisson(lam)):
             queue.append(new_req())
         return gen, prompt_tok, len(batch), int(meta.positions.shape[0])
@@ -1142,7 +1177,7 @@ def main() -> None:
     ap.add_argument("--seed", type=int, default=2026)
     ap.add_argument("--pool-frac", type=float, default=0.9)
     ap.add_argument("--max-graphs", type=int, default=32)
-    ap.add_argument("--e2e-steps", type=int, default=50)
+    ap.add_argument("--e2e-steps", type=int, default=200)
     ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU oracle timing (0 = skip)")
     ap.add_argument("--no-swap", dest="swap", action="store_false")
     ap.add_argument("--no-prefill", dest="prefill", action="store_false")

@@ -204,6 +204,57 @@ PKV_API int pkv_copy_blocks(const pkv_pool* pool, const int32_t* src, const int3
  * IndexError, paged_torch.py:199-202); src == dst is a no-op. */
 PKV_API int pkv_copy_block(const pkv_pool* pool, int64_t src, int64_t dst, void* stream);
 
+/* ---- step descriptor assembly ---------------------------------------------
+ * Replaces build_batch_meta (serving/engine_iface/batch.py:190-318) with
+ * SequenceBlocks.slots_for_new_tokens (serving/memory/block_table.py:100-121)
+ * and build_csr (block_table.py:184-208): the BatchMeta fields of one step are
+ * computed on the device from a device-resident block table whose rows hold
+ * each sequence's physical block ids in logical order. The host sends only the
+ * step's rows and lengths plus the table entries that changed. */
+typedef struct pkv_block_tables {
+  int32_t* table;      /* device [max_seqs][max_pages]: row r = one sequence's block ids */
+  int32_t max_seqs;
+  int32_t max_pages;   /* entries per row */
+  int32_t block_size;  /* tokens per page */
+  int32_t reserved;
+} pkv_block_tables;
+
+/* Device outputs, the BatchMeta fields (docs/ARCHITECTURE.md:88-120). The
+ * kernels write at most seqs_cap (+1 for the two prefix sums) / tokens_cap /
+ * pages_cap entries of the respective arrays. */
+typedef struct pkv_meta_out {
+  int32_t* query_lens;       /* [n] */
+  int32_t* cu_query_lens;    /* [n+1] exclusive prefix sum of query_lens */
+  int32_t* kv_lens;          /* [n] */
+  int64_t* positions;        /* [T] absolute positions kv_len-q_len .. kv_len-1 */
+  int32_t* last_token_ix;    /* [n] cu_query_lens[i+1] - 1 */
+  int32_t* kv_indptr;        /* [n+1] */
+  int32_t* kv_indices;       /* [sum of ceil(kv_len / block_size)] table rows, page order */
+  int32_t* kv_last_page_len; /* [n] in [1, block_size] */
+  int32_t* batch_indices;    /* [T] owning sequence of each token */
+  int32_t* slot_mapping;     /* [T] block * block_size + position % block_size */
+  int32_t seqs_cap;
+  int32_t reserved;
+  int64_t tokens_cap;
+  int64_t pages_cap;
+} pkv_meta_out;
+
+/* One step's BatchMeta. Input: int32 words rows[n] query_lens[n] kv_lens[n]
+ * upd_row[u] upd_page[u] upd_block[u], in `step_dev` (device); if `step_host`
+ * is non-NULL (pinned host memory) those 3n + 3u words are first copied from it
+ * to `step_dev` on `stream`. On the device, in stream order: the u table writes
+ * table[upd_row][upd_page] = upd_block, then every output field of the n
+ * sequences (sequence i = table row rows[i], kv_len = kv_lens[i] AFTER this
+ * step's append, query_len = query_lens[i]). PKV_ERR_ARG for an empty batch
+ * (the reference raises ValueError, batch.py:238-242) or n > seqs_cap. On the
+ * device, an update outside the table, a row outside it, query_len < 1,
+ * query_len > kv_len, a page count above max_pages, or totals above the
+ * capacities set PKV_DEV_META_BAD in *dev_status; such a sequence gets no
+ * pages and slot -1 for its tokens. */
+PKV_API int pkv_build_batch_meta(const pkv_block_tables* tables, const int32_t* step_host, int32_t* step_dev,
+                                 int32_t n_seqs, int32_t n_updates, const pkv_meta_out* out,
+                                 int32_t* dev_status, void* stream);
+
 /* ---- swap gather / scatter ------------------------------------------------
  * Replace KVSwapSpace._to_host / _from_host (serving/scheduler/preemption.py:490-523).
  * Host layout of a swapped sequence (the SwapHandle's k / v,

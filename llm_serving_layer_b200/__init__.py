@@ -10,7 +10,9 @@ Drop-ins behind the reference's own interfaces:
 * ``B200SwapSpace`` — preemption swap engine, replacing
   ``serving.scheduler.preemption.KVSwapSpace``;
 * ``BatchMeta`` / ``build_meta`` — the engine's step descriptor (field-for-field)
-  and a vectorised assembler.
+  and a vectorised host assembler;
+* ``DeviceBlockTables`` — block tables kept on the device and each step's
+  ``BatchMeta`` assembled there, replacing the engine's ``build_batch_meta``.
 
 All compute runs in ``_lib/libpkv.so`` (hand-written CUDA, C ABI in
 ``include/pkv.h``); build it with ``python -m llm_serving_layer_b200.build``.
@@ -19,6 +21,7 @@ All compute runs in ``_lib/libpkv.so`` (hand-written CUDA, C ABI in
 from .backend import B200PagedBackend
 from .meta import AttentionBackend, BatchMeta, build_meta
 from .swap import B200SwapSpace, SwapHandle, SwapSpaceFull
+from .tables import DeviceBlockTables
 
 __all__ = [
     "B200PagedBackend",
@@ -28,4 +31,5 @@ __all__ = [
     "BatchMeta",
     "AttentionBackend",
     "build_meta",
+    "DeviceBlockTables",
 ]

@@ -39,8 +39,22 @@ class BatchDesc(ctypes.Structure):
                 ("kv_indices", c_vp), ("kv_last_page_len", c_vp), ("dev_status", c_vp)]
 
 
+class BlockTablesDesc(ctypes.Structure):
+    _fields_ = [("table", c_vp), ("max_seqs", c_i32), ("max_pages", c_i32), ("block_size", c_i32),
+                ("reserved", c_i32)]
+
+
+class MetaOutDesc(ctypes.Structure):
+    _fields_ = [("query_lens", c_vp), ("cu_query_lens", c_vp), ("kv_lens", c_vp), ("positions", c_vp),
+                ("last_token_ix", c_vp), ("kv_indptr", c_vp), ("kv_indices", c_vp),
+                ("kv_last_page_len", c_vp), ("batch_indices", c_vp), ("slot_mapping", c_vp),
+                ("seqs_cap", c_i32), ("reserved", c_i32), ("tokens_cap", c_i64), ("pages_cap", c_i64)]
+
+
 P_POOL = ctypes.POINTER(PoolDesc)
 P_BATCH = ctypes.POINTER(BatchDesc)
+P_TABLES = ctypes.POINTER(BlockTablesDesc)
+P_META_OUT = ctypes.POINTER(MetaOutDesc)
 
 # name -> (restype, argtypes); every symbol include/pkv.h declares
 SIGNATURES = {
@@ -57,6 +71,7 @@ SIGNATURES = {
     "pkv_attend_decode_noalloc": (c_i32, [P_POOL, c_i32, c_i32, c_vp, c_vp, c_float, P_BATCH, c_vp]),
     "pkv_copy_blocks": (c_i32, [P_POOL, c_vp, c_vp, c_i64, c_vp, c_vp]),
     "pkv_copy_block": (c_i32, [P_POOL, c_i64, c_i64, c_vp]),
+    "pkv_build_batch_meta": (c_i32, [P_TABLES, c_vp, c_vp, c_i32, c_i32, P_META_OUT, c_vp, c_vp]),
     "pkv_swap_gather": (c_i32, [P_POOL, c_vp, c_i64, c_vp, c_vp, c_vp]),
     "pkv_swap_scatter": (c_i32, [P_POOL, c_vp, c_i64, c_vp, c_vp, c_vp]),
     "pkv_swapper_create": (c_i32, [c_vp, c_size, ctypes.POINTER(c_vp)]),

@@ -299,12 +299,17 @@ class B200PagedBackend:
         # hint for the attention entry point: 1 = every query length is 1 (decode
         # kernel), 2 = none is (pure prefill), 0 = unknown / mixed (the q_len == 1
         # rows of a mixed batch run on the decode kernel)
-        if self.validate == "host":
+        checked = int(getattr(meta, "checked_blocks", 0) or 0)
+        if self.validate == "host" and not (0 < checked <= self.num_blocks
+                                            and getattr(meta, "max_query_len", None) is not None):
             decode, hint = self._host_validate(meta, n, total_pages)
         else:
+            # device validation, or an assembler that made the host checks already
+            # (DeviceBlockTables: lengths, page counts, block ids inside this pool)
             mql = getattr(meta, "max_query_len", None)
+            mnql = getattr(meta, "min_query_len", None)
             decode = (int(mql) == 1) if mql is not None else not bool(meta.is_prefill)
-            hint = 1 if decode else 0
+            hint = 1 if decode else (2 if mnql is not None and int(mnql) > 1 else 0)
         if decode and n_tokens != n:
             raise ValueError(
                 f"BatchMeta describes a decode step (is_prefill=False) but has {n_tokens} tokens for "

@@ -111,6 +111,32 @@ __device__ __forceinline__ void flag(int32_t* st, int32_t bits) {
   if (st) atomicOr(st, bits);
 }
 
+// Exclusive prefix sum of v over the CTA (every thread calls it); *total gets the sum.
+__device__ __forceinline__ int block_excl_scan(int v, int* warp_sum, int* total) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+  int incl = v;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const int u = __shfl_up_sync(0xffffffffu, incl, off);
+    if (lane >= off) incl += u;
+  }
+  __syncthreads();
+  if (lane == 31) warp_sum[w] = incl;
+  __syncthreads();
+  if (w == 0) {
+    int x = lane < nw ? warp_sum[lane] : 0;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int u = __shfl_up_sync(0xffffffffu, x, off);
+      if (lane >= off) x += u;
+    }
+    warp_sum[lane] = x;
+  }
+  __syncthreads();
+  *total = warp_sum[nw - 1];
+  return (w ? warp_sum[w - 1] : 0) + incl - v;
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

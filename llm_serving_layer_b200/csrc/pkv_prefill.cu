@@ -65,32 +65,6 @@ __device__ __forceinline__ int tile_pages(int64_t kv, int ql, int j0, int qt) {
   return int(c < 0x7fffffff ? c : 0x7fffffff);
 }
 
-// Exclusive prefix sum of v over the CTA (every thread calls it); *total gets the sum.
-__device__ __forceinline__ int block_excl_scan(int v, int* warp_sum, int* total) {
-  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
-  int incl = v;
-#pragma unroll
-  for (int off = 1; off < 32; off <<= 1) {
-    const int u = __shfl_up_sync(0xffffffffu, incl, off);
-    if (lane >= off) incl += u;
-  }
-  __syncthreads();
-  if (lane == 31) warp_sum[w] = incl;
-  __syncthreads();
-  if (w == 0) {
-    int x = lane < nw ? warp_sum[lane] : 0;
-#pragma unroll
-    for (int off = 1; off < 32; off <<= 1) {
-      const int u = __shfl_up_sync(0xffffffffu, x, off);
-      if (lane >= off) x += u;
-    }
-    warp_sum[lane] = x;
-  }
-  __syncthreads();
-  *total = warp_sum[nw - 1];
-  return (w ? warp_sum[w - 1] : 0) + incl - v;
-}
-
 // Decode rows of a mixed batch, for the decode kernel: the q_len == 1
 // sequences are listed contiguously (index d), their pages get the decode
 // kernel's descriptors {page id, d<<7 | first<<6 | last<<5 | valid, first page

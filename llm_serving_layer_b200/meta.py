@@ -44,6 +44,13 @@ class BatchMeta:
     kv_last_page_len (n,)  int32  occupancy of the last page, in [1, page_size]
     batch_indices   (T,)   int32  owning sequence of each token
     slot_mapping    (T,)   int32  flat physical slot of each new token, or None
+
+    Optional host-side facts, known to an assembler without reading the device
+    tensors back (``None`` / 0 when not supplied): ``max_query_len`` and
+    ``min_query_len``, and ``checked_blocks`` — when nonzero, the assembler has
+    already made the page-table checks a backend would otherwise make by reading
+    the fields back (query and kv lengths, page counts) and every block id in
+    the page table lies in ``[0, checked_blocks)``.
     """
 
     query_lens: torch.Tensor
@@ -58,6 +65,9 @@ class BatchMeta:
     slot_mapping: torch.Tensor | None = None
     page_size: int = 16
     is_prefill: bool = False
+    max_query_len: int | None = None
+    min_query_len: int | None = None
+    checked_blocks: int = 0
 
     @property
     def n_seqs(self) -> int:
@@ -204,4 +214,6 @@ def build_meta(
         slot_mapping=put(slots, i32),
         page_size=int(page_size),
         is_prefill=bool((ql > 1).any()),
+        max_query_len=int(ql.max()),
+        min_query_len=int(ql.min()),
     )
