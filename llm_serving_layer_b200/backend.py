@@ -306,9 +306,11 @@ class B200PagedBackend:
         else:
             # device validation, or an assembler that made the host checks already
             # (DeviceBlockTables: lengths, page counts, block ids inside this pool)
+            # is_prefill decides decode vs not (a batch mislabelled as decode is
+            # refused below); the query-length bounds only sharpen the hint
             mql = getattr(meta, "max_query_len", None)
             mnql = getattr(meta, "min_query_len", None)
-            decode = (int(mql) == 1) if mql is not None else not bool(meta.is_prefill)
+            decode = not bool(meta.is_prefill) if hasattr(meta, "is_prefill") else int(mql) == 1
             hint = 1 if decode else (2 if mnql is not None and int(mnql) > 1 else 0)
         if decode and n_tokens != n:
             raise ValueError(

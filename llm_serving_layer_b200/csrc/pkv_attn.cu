@@ -12,11 +12,14 @@
 //                   per-warp TMA ring (128B-swizzled, mbarrier-completed) and
 //                   does the math on tensor cores (S^T = K.Q^T, O^T += V^T.P^T,
 //                   m16n8k16, fp32 accumulate) with an fp32 online softmax.
-//                   Sequences cut by a range boundary are merged per KV head:
-//                   each consumer warp publishes its heads' partial and counts
-//                   it in (one atomic counter per (sequence, KV head)); the
-//                   warp that completes the count merges those heads (no
-//                   waiting, no CTA-wide barrier).
+//                   A sequence cut by a range boundary leaves a piece at each
+//                   end of the ranges it touches; the consumer warps hand their
+//                   heads' piece to the CTA's merge warp through shared memory
+//                   and move on, and the merge warp publishes it, counts it in
+//                   (one atomic counter per sequence) and, if that completes
+//                   the count, merges the sequence's pieces — off the
+//                   streaming warps' path. A range's cut pieces are processed
+//                   first, so their merges overlap the rest of its pages.
 //   generic_kernel  any geometry / dtype the tensor-core kernels (decode here,
 //                   prefill in pkv_prefill.cu) do not take: one warp per
 //                   (token, query head), CUDA cores.
@@ -38,15 +41,16 @@ constexpr int DK_NST = 6;                  // default ring depth (pages in fligh
 constexpr int DK_KV_MAX = 8;               // KV heads of the decode kernel (one consumer warp each)
 constexpr int DK_WMERGE = 4;               // split-K pieces fetched per round of loads in a merge
 constexpr int DK_U = 2;                    // pages folded per online-softmax update
+constexpr int DK_PREFETCH = 8;             // pages a CTA prefetches into L2 before the earlier kernel is done
 #ifndef DK_PRODUCER_SLEEP_NS
 #define DK_PRODUCER_SLEEP_NS 64            // producer back-off while the ring is full
 #endif
-constexpr int DK_MAXNREG = 168;            // 9 warps: 3 per SM sub-partition x 32 x 168 <= 16K registers
+constexpr int DK_MAXNREG = 168;            // 10 warps: <= 3 per SM sub-partition x 32 x 168 <= 16K registers
 
 // ---------------------------------------------------------------- workspace
 struct WsLayout {
   size_t page_desc = 0;  // int4[total_pages]
-  size_t counters = 0;   // int32[n_seqs][DK_KV_MAX]: split pieces counted in, per (seq, KV head)
+  size_t counters = 0;   // int32[n_seqs]: split pieces counted in, per sequence
   size_t partial_o = 0;   // float[2 * grid][n_heads][D]
   size_t partial_ml = 0;  // float2[2 * grid][n_heads]
   size_t n_tiles = 0;     // int32: prefill tiles planned (prefill layout only)
@@ -67,7 +71,7 @@ WsLayout ws_layout(int n_heads, int n_seqs, int64_t total_pages, int max_grid, i
   w.page_desc = off;
   off = align256(off + sizeof(int4) * size_t(std::max<int64_t>(total_pages, 1)));
   w.counters = off;
-  off = align256(off + sizeof(int32_t) * DK_KV_MAX * size_t(std::max(n_seqs, 1)));
+  off = align256(off + sizeof(int32_t) * size_t(std::max(n_seqs, 1)));
   w.partial_o = off;
   off = align256(off + sizeof(float) * size_t(2) * max_grid * n_heads * head_dim);
   w.partial_ml = off;
@@ -100,7 +104,7 @@ __global__ void plan_kernel(const int32_t* __restrict__ kv_indptr,
   const int lane = threadIdx.x & 31;
   if (warp >= n_seqs) return;
   const int s = warp;
-  if (lane < DK_KV_MAX) counters[size_t(s) * DK_KV_MAX + lane] = 0;
+  if (lane == 0) counters[s] = 0;
   const int64_t a = kv_indptr[s], b = kv_indptr[s + 1];
   const int lpl = last_page_len[s];
   bool bad = (a > b) || (b > total_pages) || (lpl < 1) || (lpl > block_size);
@@ -152,6 +156,7 @@ struct DecodeArgs {
   int n_heads;
   int layer;
   float scale_log2;
+  int prefetch;          // pages of the range warmed in L2 before the earlier kernel completed (<= 32)
 };
 
 __host__ __device__ constexpr size_t bar_bytes(int n_warps, int nst) {
@@ -179,17 +184,18 @@ __device__ __forceinline__ void load_q_frag(const T* __restrict__ q, int row, in
   }
 }
 
-// Warp h merges the split-K pieces in CTAs cf..cl of a sequence (output row
-// `row`) for its query heads h*GROUPS .. h*GROUPS + GROUPS - 1. Its own piece (CTA `own`) is
-// still in `ostage` (O/l, fp32, [GROUPS][64]) with (m, l) given per lane for
-// the head its elements belong to; every other piece's O/l and (m, l) are read
-// from the workspace, DK_WMERGE pieces per round of loads. Pieces are folded in
+// Consumer warp h merges the split-K pieces in CTAs cf..cl of a sequence
+// (output row `row`) for its query heads h*GROUPS .. h*GROUPS + GROUPS - 1. Its
+// own CTA's piece (CTA `own`) is still in the handoff slot: `ostage` (O/l, fp32,
+// [GROUPS][64], this warp's heads) and `oml` ((m, l) per head); every other
+// piece's O/l and (m, l) are read from the workspace, DK_WMERGE pieces per round
+// of loads. Pieces are folded in
 // CTA order with weights l * 2^(m - M) whichever warp merges, so the result is
 // the same bits run after run. Lane `lane` owns elements [lane*PER, lane*PER + PER).
 template <typename T, int GROUPS>
 __device__ __forceinline__ void merge_warp(const DecodeArgs& a, int row, int h, int own, int64_t fa,
                                            int cf, int cl, int64_t P, int G, const float* ostage,
-                                           float om, float ol, int lane) {
+                                           const float2* oml, int lane) {
   constexpr int PER = GROUPS * DK_D / 32;  // 2, 4, 8 or 16 elements per lane
   const int nh = a.n_heads;
   const int e0 = lane * PER;
@@ -209,7 +215,7 @@ __device__ __forceinline__ void merge_warp(const DecodeArgs& a, int row, int h, 
 #pragma unroll
       for (int r = 0; r < PER; ++r) v[u][r] = 0.f;
       if (cc == own) {
-        ml[u] = make_float2(om, ol);
+        ml[u] = oml[j];
 #pragma unroll
         for (int r = 0; r < PER; ++r) v[u][r] = ostage[e0 + r];
       } else if (cc <= cl) {
@@ -344,9 +350,13 @@ __device__ __forceinline__ void attend_pages(const uint32_t (&kb)[U], const uint
 // with the 128B swizzle keyed on the token (conflict-free ldmatrix over a
 // head's 16 tokens). Consumer warp h reads its head's 2 KiB slice of each stage
 // and walks the range sequence piece by sequence piece, DK_U pages per
-// online-softmax update. A piece cut by a range boundary is written as a
-// partial (O/l, m, l) per consumer warp and counted in with one atomic per
-// (sequence, KV head); the warp that completes a count merges those heads.
+// online-softmax update. A range holds at most two pieces cut by its ends (the
+// piece at p0 and the one at p1); they are processed first (the one at p1,
+// then the one at p0, then the sequences inside), and each consumer warp writes
+// its heads' (O/l, m, l) of such a piece into that piece's handoff slot in
+// shared memory and moves on. The merge warp takes each slot when all consumer
+// warps arrived, publishes it to the workspace, counts it in with one atomic
+// per sequence and, if that completed the count, merges the sequence.
 // FUSE: the variant with the KV-append folded in (DecodeArgs::knew set); a
 // separate instantiation, so the plain decode kernel carries none of its code.
 template <typename T, int GROUPS, int NST, bool FUSE>
@@ -355,7 +365,7 @@ __global__ void __maxnreg__(DK_MAXNREG) decode_kernel(const __grid_constant__ CU
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const int n_cons = (blockDim.x >> 5) - 1;  // consumer warps == KV heads
+  const int n_cons = (blockDim.x >> 5) - 2;  // consumer warps == KV heads; then producer, merge warp
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, c4 = lane & 3;
   constexpr int PAGE = DK_P * DK_D * 8 * 2;  // 16 KiB: one page of one layer, K or V (8 heads)
@@ -363,13 +373,35 @@ __global__ void __maxnreg__(DK_MAXNREG) decode_kernel(const __grid_constant__ CU
   unsigned char* stages = smem;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + size_t(NST) * STAGE);
   uint64_t* empty = full + NST;
-  float* ostage_all = reinterpret_cast<float*>(smem + size_t(NST) * STAGE + bar_bytes(2, NST));
+  uint64_t* hbar = empty + NST;  // [2]: the handoff slots' consumer arrivals
+  const int nh = a.n_heads;
+  float* ostage_all = reinterpret_cast<float*>(smem + size_t(NST) * STAGE + bar_bytes(2, NST + 1));
+  float* hand = ostage_all + size_t(nh) * DK_D;                  // [2][n_heads][64] O/l of the cut pieces
+  float2* hml = reinterpret_cast<float2*>(hand + size_t(2) * nh * DK_D);  // [2][n_heads] (m, l)
+  int4* mjob = reinterpret_cast<int4*>(hml + 2 * nh);            // [2] {row or -1, cf, cl, fa} of a merge
+  int* mstate = reinterpret_cast<int*>(mjob + 2);                // [2] 1 once the merge warp decided
 
-  // pages to cover: the decode rows of a mixed batch are listed by the plan on
-  // the device, so their count is read here (bounded by the descriptor capacity)
+  if (threadIdx.x == 0) {
+    prefetch_tmap(&tmap);
+    for (int i = 0; i < NST; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], n_cons);
+    }
+    mbar_init(&hbar[0], n_cons);
+    mbar_init(&hbar[1], n_cons);
+    mstate[0] = mstate[1] = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
   pdl_trigger();
-  if (threadIdx.x == 0) prefetch_tmap(&tmap);
-  pdl_wait();  // the plan, q and this step's append are written by earlier kernels
+
+  // Up to pdl_wait() this CTA may run while the kernel before it (an append, the
+  // previous layer's attention) still runs. It reads only what the step's plan
+  // wrote — the plan kernel lets nothing start before it completed — and warms
+  // L2 with its first pages, which is harmless whatever the earlier kernel
+  // writes (the loads below go through the same L2).
+  // Pages to cover: the decode rows of a mixed batch are listed by the plan on
+  // the device, so their count is read there (bounded by the descriptor capacity).
   // The ranges are cut over G = min(grid, P) CTAs, so every range is non-empty
   // (a split sequence's pieces are exactly the CTAs cf..cl); surplus CTAs exit.
   const int64_t P = a.p_dev ? max(int64_t(0), min(*a.p_dev, a.total_pages)) : a.total_pages;
@@ -379,21 +411,40 @@ __global__ void __maxnreg__(DK_MAXNREG) decode_kernel(const __grid_constant__ CU
   const int64_t p0 = int64_t(c) * P / G, p1 = int64_t(c + 1) * P / G;
   if (p0 >= p1) return;
   const int R = int(p1 - p0);
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < NST; ++i) {
-      mbar_init(&full[i], 1);
-      mbar_init(&empty[i], n_cons);
-    }
-    fence_mbar_init();
-  }
-  __syncthreads();
 
-  // The range is processed in page order: its first sequence (possibly cut at
-  // p0, its piece published for the merge), the sequences inside it, its last
-  // (possibly cut at p1).
-  const int4 dfirst = a.desc[p0];
-  auto pos = [&](int i) -> int64_t { return p0 + i; };  // processing step -> page index
-  auto seg_end = [&](int i) -> int64_t { return p1; };  // one past the range's last page
+  // Processing order. The range's last sequence (tail piece T) and first
+  // sequence (head piece H) may be cut by the range's ends; T is taken first,
+  // then H, then the middle M, so that cut pieces are handed to the merge warp
+  // early and their merges overlap the consumers' remaining pages.
+  const int4 dfirst = a.desc[p0], dlast = a.desc[p1 - 1];
+  const int sf = dfirst.y >> 7, sl = dlast.y >> 7;
+  int lenT = 0, lenH = 0;
+  int64_t hend = p0, tstart = p1;
+  if (sf >= 0 && sl >= 0 && sf != sl && dfirst.w > p0 && dfirst.w <= p1 && dlast.z >= p0 && dlast.z < p1) {
+    hend = dfirst.w;
+    tstart = dlast.z;
+    lenT = int(p1 - tstart);
+    lenH = int(hend - p0);
+  }
+  auto pos = [&](int i) -> int64_t {  // processing step -> page index
+    if (i < lenT) return tstart + i;
+    if (i < lenT + lenH) return p0 + (i - lenT);
+    return (lenT ? hend : p0) + (i - lenT - lenH);
+  };
+  auto seg_end = [&](int i) -> int64_t {  // one past the last page of step i's segment
+    if (i < lenT) return p1;
+    if (i < lenT + lenH) return hend;
+    return lenT ? tstart : p1;
+  };
+  const int kv_coord = 2 * a.layer;
+  if (warp == n_cons && lane < min(R, a.prefetch)) {
+    const int id = a.desc[pos(lane)].x;
+    if (id >= 0) {
+      tma_prefetch_l2_4d(&tmap, 0, id * DK_P, 0, kv_coord);
+      tma_prefetch_l2_4d(&tmap, 0, id * DK_P, 0, kv_coord + 1);
+    }
+  }
+  pdl_wait();  // q, this step's appended rows and the split-K counters are written by earlier kernels
   // page descriptors: lane j holds window entries [wb + j] (cur) and [wb + 32 + j] (nxt)
   int wb = 0;
   int4 dcur = make_int4(-1, -1, -1, -1), dnxt = make_int4(-1, -1, -1, -1);
@@ -416,7 +467,56 @@ __global__ void __maxnreg__(DK_MAXNREG) decode_kernel(const __grid_constant__ CU
       if (wb + 32 + lane < R) dnxt = a.desc[pos(wb + 32 + lane)];
     }
   };
-  const int kv_coord = 2 * a.layer;
+
+  auto row_ok = [&](const int4& d, int& row) -> bool {  // the consumers' test of a piece's first page
+    const int sq = d.y >> 7;
+    row = (sq >= 0 && sq < a.n_seqs) ? (a.rows ? __ldg(a.rows + sq) : sq) : -1;
+    return row >= 0 && row < a.n_rows && (d.y & 31) >= 1 && (d.y & 31) <= DK_P;
+  };
+
+  // the range's pieces cut by its ends: A (the piece at p0, handoff slot 0) and
+  // B (the piece at p1, slot 1)
+  int rA, rB;
+  const bool cutA = row_ok(dfirst, rA) && (dfirst.z < p0 || dfirst.w > p1);
+  const bool cutB = sl != sf && row_ok(dlast, rB) && dlast.w > p1;
+
+  if (warp == n_cons + 1) {
+    // ---------------- merge warp: publish each cut piece, count it in, and if
+    // that completed the sequence, post the merge for the consumer warps
+    for (int t = 0; t < 2; ++t) {
+      const int slot = (lenT > 0) ? 1 - t : t;  // in processing order: T (slot 1) first when reordered
+      if (!(slot == 0 ? cutA : cutB)) continue;
+      const int4 d = slot == 0 ? dfirst : dlast;
+      const int seq = d.y >> 7, row = slot == 0 ? rA : rB;
+      const int64_t fa = d.z, fb = d.w;
+      const int cf = cta_of(fa, P, G), cl = cta_of(fb - 1, P, G);
+      int job_row = -1;
+      if (mbar_wait_bounded_sleepy(&hbar[slot], 0, a.st, DK_PRODUCER_SLEEP_NS)) {
+        const float* ho = hand + size_t(slot) * nh * DK_D;
+        const float2* hm = hml + size_t(slot) * nh;
+        float* po = a.partial_o + size_t(2 * c + slot) * nh * DK_D;
+        for (int e = lane * 4; e < nh * DK_D; e += 32 * 4)
+          __stcg(reinterpret_cast<float4*>(po + e), *reinterpret_cast<const float4*>(ho + e));
+        for (int j = lane; j < nh; j += 32) __stcg(a.partial_ml + size_t(2 * c + slot) * nh + j, hm[j]);
+        __syncwarp();
+        int prev = 0;
+        int32_t* cnt = a.counters + seq;
+        if (lane == 0) asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], 1;" : "=r"(prev) : "l"(cnt) : "memory");
+        prev = __shfl_sync(0xffffffffu, prev, 0);
+        if (prev == cl - cf) {  // every piece is in: this CTA merges; the count restarts at 0
+          job_row = row;
+          if (lane == 0) *cnt = 0;
+        }
+      }
+      if (lane == 0) {
+        mjob[slot] = make_int4(job_row, cf, cl, int(fa));
+        __threadfence_block();
+        *reinterpret_cast<volatile int*>(&mstate[slot]) = 1;
+      }
+      __syncwarp();
+    }
+    return;
+  }
 
   if (warp == n_cons) {
     // ---------------- producer warp
@@ -493,6 +593,35 @@ __global__ void __maxnreg__(DK_MAXNREG) decode_kernel(const __grid_constant__ CU
     __syncwarp();
   };
 
+  // merges posted by the merge warp, done by every consumer warp for its heads:
+  // polled between pieces, and waited for (bounded) once the range is done
+  int mdone = (cutA ? 0 : 1) | (cutB ? 0 : 2);
+  auto run_merges = [&](bool wait) {
+    for (int ms = 0; ms < 2; ++ms) {
+      if ((mdone >> ms) & 1) continue;
+      int ready = 0;
+      if (lane == 0) {
+        volatile int* f = &mstate[ms];
+        ready = *f;
+        if (!ready && wait) {
+          const uint64_t t0 = globaltimer_ns();
+          while (!(ready = *f) && globaltimer_ns() - t0 < 1000000000ull) __nanosleep(64);
+          if (!ready) flag(a.st, PKV_DEV_WAIT_TIMEOUT);
+        }
+      }
+      ready = __shfl_sync(0xffffffffu, ready, 0);
+      if (!ready && !wait) continue;
+      mdone |= 1 << ms;
+      if (!ready) continue;
+      __threadfence_block();
+      const int4 j = mjob[ms];
+      if (j.x >= 0)
+        merge_warp<T, GROUPS>(a, j.x, h, c, j.w, j.y, j.z, P, G,
+                              hand + size_t(ms) * nh * DK_D + size_t(h) * GROUPS * DK_D,
+                              hml + size_t(ms) * nh + h * GROUPS, lane);
+    }
+  };
+
   uint32_t qb[4][2], qn[4][2];
   int nxt_seq = -1, nxt_row = -1;
   auto row_of = [&](int sq) -> int { return a.rows ? __ldg(a.rows + sq) : sq; };
@@ -526,7 +655,7 @@ __global__ void __maxnreg__(DK_MAXNREG) decode_kernel(const __grid_constant__ CU
       load_q_frag<T, GROUPS>(q, row, a.n_heads, h, g, c4, qb);
     }
     // the sequence processed next: H's after T, then each M in turn
-    nxt_seq = seq + 1;
+    nxt_seq = (i < lenT) ? sf : seq + 1;
     nxt_row = (nxt_seq >= 0 && nxt_seq < a.n_seqs) ? row_of(nxt_seq) : -1;
     if (nxt_row >= 0 && nxt_row < a.n_rows) load_q_frag<T, GROUPS>(q, nxt_row, a.n_heads, h, g, c4, qn);
     else nxt_seq = -1;
@@ -569,7 +698,11 @@ __global__ void __maxnreg__(DK_MAXNREG) decode_kernel(const __grid_constant__ CU
     }
     i += n;
 
-    // finalise the piece: normalise (O/l) into this warp's staging slice
+    // finalise the piece: normalise (O/l) into this warp's staging slice (a
+    // whole sequence) or into its heads' part of the piece's handoff slot
+    const bool whole = seen_first && ends_here;
+    const int slot = (seq == first_seq) ? 0 : 1;
+    float* fin = whole ? ostage : hand + size_t(slot) * nh * DK_D + size_t(h) * GROUPS * DK_D;
     float lt0 = l0, lt1 = l1;
 #pragma unroll
     for (int off = 4; off < 32; off <<= 1) {
@@ -582,61 +715,44 @@ __global__ void __maxnreg__(DK_MAXNREG) decode_kernel(const __grid_constant__ CU
     for (int mt = 0; mt < 4; ++mt) {
       const int d0 = mt * 16 + g, d1 = d0 + 8;
       if (j0 < GROUPS) {
-        ostage[j0 * DK_D + d0] = o[mt][0] * i0;
-        ostage[j0 * DK_D + d1] = o[mt][2] * i0;
+        fin[j0 * DK_D + d0] = o[mt][0] * i0;
+        fin[j0 * DK_D + d1] = o[mt][2] * i0;
       }
       if (j1 < GROUPS) {
-        ostage[j1 * DK_D + d0] = o[mt][1] * i1;
-        ostage[j1 * DK_D + d1] = o[mt][3] * i1;
+        fin[j1 * DK_D + d0] = o[mt][1] * i1;
+        fin[j1 * DK_D + d1] = o[mt][3] * i1;
       }
     }
-    __syncwarp();
-    if (seen_first && ends_here) {
-      // the whole sequence lives in this CTA: store it in the pool dtype
-      T* dst = out + (int64_t(row) * a.n_heads + h * GROUPS) * DK_D;
-      for (int e = lane * 8; e < GROUPS * DK_D; e += 32 * 8) {
-        const float4 x = *reinterpret_cast<const float4*>(ostage + e);
-        const float4 y = *reinterpret_cast<const float4*>(ostage + e + 4);
-        uint4 v;
-        v.x = MmaOp<T>::pack(x.x, x.y);
-        v.y = MmaOp<T>::pack(x.z, x.w);
-        v.z = MmaOp<T>::pack(y.x, y.y);
-        v.w = MmaOp<T>::pack(y.z, y.w);
-        *reinterpret_cast<uint4*>(dst + e) = v;
+    if (!whole) {
+      // a piece cut by a range end: hand it to the merge warp and move on
+      if (g == 0) {
+        float2* hm = hml + size_t(slot) * nh + h * GROUPS;
+        if (j0 < GROUPS) hm[j0] = make_float2(m0, lt0);
+        if (j1 < GROUPS) hm[j1] = make_float2(m1, lt1);
       }
       __syncwarp();
+      if (lane == 0)
+        asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&hbar[slot])) : "memory");
+      run_merges(false);
       continue;
     }
-    // a piece of a sequence cut by a range boundary: publish this warp's heads'
-    // (O/l, m, l), count the piece in for this KV head, and if that completes
-    // the count, merge these heads' pieces right here (no CTA-wide barrier)
-    const int slot = (seq == first_seq) ? 0 : 1;
-    float* po = a.partial_o + (size_t(2 * c + slot) * a.n_heads + h * GROUPS) * DK_D;
-    for (int e = lane * 4; e < GROUPS * DK_D; e += 32 * 4)
-      __stcg(reinterpret_cast<float4*>(po + e), *reinterpret_cast<const float4*>(ostage + e));
-    if (g == 0) {
-      float2* pml = a.partial_ml + size_t(2 * c + slot) * a.n_heads + h * GROUPS;
-      if (j0 < GROUPS) pml[j0] = make_float2(m0, lt0);
-      if (j1 < GROUPS) pml[j1] = make_float2(m1, lt1);
+    __syncwarp();
+    // the whole sequence lives in this CTA: store it in the pool dtype
+    T* dst = out + (int64_t(row) * a.n_heads + h * GROUPS) * DK_D;
+    for (int e = lane * 8; e < GROUPS * DK_D; e += 32 * 8) {
+      const float4 x = *reinterpret_cast<const float4*>(ostage + e);
+      const float4 y = *reinterpret_cast<const float4*>(ostage + e + 4);
+      uint4 v;
+      v.x = MmaOp<T>::pack(x.x, x.y);
+      v.y = MmaOp<T>::pack(x.z, x.w);
+      v.z = MmaOp<T>::pack(y.x, y.y);
+      v.w = MmaOp<T>::pack(y.z, y.w);
+      *reinterpret_cast<uint4*>(dst + e) = v;
     }
     __syncwarp();
-    const int64_t fa = d.z, fb = d.w;
-    const int cf = cta_of(fa, P, G), cl = cta_of(fb - 1, P, G);
-    int prev = 0;
-    int32_t* cnt = a.counters + size_t(seq) * DK_KV_MAX + h;
-    if (lane == 0) asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], 1;" : "=r"(prev) : "l"(cnt) : "memory");
-    prev = __shfl_sync(0xffffffffu, prev, 0);
-    __syncwarp();
-    if (prev == cl - cf) {
-      // this lane's head is j = lane * PER / 64; its (m, l) sit in lane j / 2 (column j & 1)
-      const int jh = (lane * GROUPS * DK_D / 32) / DK_D;
-      const float mA = __shfl_sync(0xffffffffu, m0, jh >> 1), mB = __shfl_sync(0xffffffffu, m1, jh >> 1);
-      const float lA = __shfl_sync(0xffffffffu, lt0, jh >> 1), lB = __shfl_sync(0xffffffffu, lt1, jh >> 1);
-      merge_warp<T, GROUPS>(a, row, h, c, fa, cf, cl, P, G, ostage, (jh & 1) ? mB : mA, (jh & 1) ? lB : lA, lane);
-      if (lane == 0) *cnt = 0;
-    }
-    __syncwarp();
+    run_merges(false);
   }
+  run_merges(true);
 }
 
 // ---------------------------------------------------------------- generic
@@ -850,17 +966,34 @@ bool decode_supported(const pkv_pool& p, int n_heads) {
 
 size_t decode_smem(int n_kv_heads, int groups, int nst) {
   const size_t stage = size_t(2) * DK_P * DK_D * 8 * 2;  // K + V page, 8 heads (boxes always 8 wide)
-  return 1024 + nst * stage + bar_bytes(2, nst) + size_t(n_kv_heads) * groups * DK_D * 4;
+  const size_t nh = size_t(n_kv_heads) * groups;
+  // ring, barriers, staging slices, two handoff slots (O/l and (m, l)), merge jobs
+  return 1024 + nst * stage + bar_bytes(2, nst + 1) + nh * DK_D * 4 + 2 * nh * DK_D * 4 + 2 * nh * 8 +
+         2 * sizeof(int4) + 16;
 }
 
-// Ring depth and CTAs per SM of the decode kernel. Defaults are the tuned
-// values; PKV_DECODE_NST (3, 4, 5 or 6) and PKV_DECODE_CTAS_PER_SM override them
-// for launch-shape sweeps.
+// Ring depth, L2 prefetch depth and CTAs per SM of the decode kernel. Defaults
+// are the tuned values; PKV_DECODE_NST (3, 4, 5 or 6), PKV_DECODE_PREFETCH
+// (0-32 pages) and PKV_DECODE_CTAS_PER_SM override them for sweeps.
 int decode_nst() {
   static int v = [] {
     const char* e = getenv("PKV_DECODE_NST");
     const int n = e ? atoi(e) : DK_NST;
     return (n == 3 || n == 4 || n == 5 || n == 6) ? n : DK_NST;
+  }();
+  return v;
+}
+// the deepest ring (<= the requested depth) whose shared memory fits a CTA
+int decode_nst_for(int n_kv_heads, int groups) {
+  int n = decode_nst();
+  while (n > 3 && decode_smem(n_kv_heads, groups, n) > size_t(232448)) --n;
+  return n;
+}
+int decode_prefetch() {
+  static int v = [] {
+    const char* e = getenv("PKV_DECODE_PREFETCH");
+    const int n = e ? atoi(e) : DK_PREFETCH;
+    return (n >= 0 && n <= 32) ? n : DK_PREFETCH;
   }();
   return v;
 }
@@ -890,7 +1023,7 @@ int decode_grid_limit(int n_kv_heads) {
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm));
     int v = 0;
     if (e == cudaSuccess)
-      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, fn, 32 * (n_kv_heads + 1), sm);
+      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, fn, 32 * (n_kv_heads + 2), sm);
     if (e != cudaSuccess) {
       cuda_fail(e, "decode kernel occupancy query");
       return -1;
@@ -909,7 +1042,8 @@ int launch_decode_f(const pkv_pool& p, const CUtensorMap& tm, DecodeArgs& a, int
   if (limit <= 0) return PKV_ERR_CUDA;  // message already set
   limit = std::min(limit, max_decode_grid());
   const int grid = int(std::max<int64_t>(1, std::min<int64_t>(limit, total_pages)));
-  PKV_CUDA_RET(launch_kernel(decode_kernel<T, GROUPS, NST, FUSE>, dim3(grid), dim3(32 * (p.n_kv_heads + 1)),
+  a.prefetch = decode_prefetch();
+  PKV_CUDA_RET(launch_kernel(decode_kernel<T, GROUPS, NST, FUSE>, dim3(grid), dim3(32 * (p.n_kv_heads + 2)),
                              decode_smem(p.n_kv_heads, GROUPS, NST), s, true, tm, a));
   return PKV_OK;
 }
@@ -923,7 +1057,7 @@ int launch_decode_t(const pkv_pool& p, const CUtensorMap& tm, DecodeArgs& a, int
 template <typename T, int GROUPS>
 int launch_decode_n(const pkv_pool& p, const CUtensorMap& tm, DecodeArgs& a, int64_t tp,
                     cudaStream_t s) {
-  switch (decode_nst()) {
+  switch (decode_nst_for(p.n_kv_heads, GROUPS)) {
     case 3: return launch_decode_t<T, GROUPS, 3, 1>(p, tm, a, tp, s);
     case 5: return launch_decode_t<T, GROUPS, 5, 1>(p, tm, a, tp, s);
     case 6: return launch_decode_t<T, GROUPS, 6, 1>(p, tm, a, tp, s);
@@ -1261,7 +1395,7 @@ int noalloc_scratch(void** out) {
 // query the launch uses), so the scratch layout covers every CTA's partials.
 template <typename T, int GROUPS>
 int decode_grid_cap_n(const pkv_pool& p) {
-  switch (decode_nst()) {
+  switch (decode_nst_for(p.n_kv_heads, GROUPS)) {
     case 3: return decode_grid_limit<T, GROUPS, 3, false>(p.n_kv_heads);
     case 5: return decode_grid_limit<T, GROUPS, 5, false>(p.n_kv_heads);
     case 6: return decode_grid_limit<T, GROUPS, 6, false>(p.n_kv_heads);

@@ -86,7 +86,7 @@ int64_t prefill_tiles_cap(int n_seqs, int64_t total_pages);
 // (workspace regions; see pkv_attn.cu's workspace layout).
 struct PrefillMixedPlan {
   int4* desc;          // [total_pages] page descriptors of the listed decode rows
-  int32_t* counters;   // [n_seqs][8] split-K counters
+  int32_t* counters;   // [n_seqs] split-K counters
   int32_t* rows;       // [n_seqs] q / out row of each listed sequence, -1 past the list
   int64_t* p_dec;      // pages listed
 };
@@ -225,6 +225,15 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, u
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2),
       "r"(c3)
       : "memory");
+}
+
+// Prefetch of a 4-D tile into L2 (no shared memory written, no completion to
+// wait for): warms the cache for a later tma_load_4d of the same tile.
+__device__ __forceinline__ void tma_prefetch_l2_4d(const CUtensorMap* map, int c0, int c1, int c2, int c3) {
+  asm volatile("cp.async.bulk.prefetch.tensor.4d.L2.global.tile [%0, {%1, %2, %3, %4}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+               : "memory");
 }
 
 // warp-level tensor-core helpers (fp16 / bf16 operands, fp32 accumulate) ----

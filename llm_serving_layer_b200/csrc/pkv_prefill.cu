@@ -69,13 +69,14 @@ __device__ __forceinline__ int tile_pages(int64_t kv, int ql, int j0, int qt) {
 // sequences are listed contiguously (index d), their pages get the decode
 // kernel's descriptors {page id, d<<7 | first<<6 | last<<5 | valid, first page
 // of d, one past its last page} in listed order, rows[d] = their q / out row,
-// rows past the list = -1, *p_dec = pages listed; split-K counters zeroed.
+// rows past the list = -1, *p_dec = pages listed; split-K counters (one per
+// listed sequence) zeroed.
 struct MixedOut {
   const int32_t* kv_indices;
   const int32_t* kv_lens;
   int64_t total_pages, num_blocks;
   int4* desc;
-  int32_t* counters;  // [n_seqs][8]
+  int32_t* counters;  // [n_seqs]
   int32_t* rows;      // [n_seqs]
   int64_t* p_dec;
 };
@@ -182,8 +183,7 @@ __global__ void __launch_bounds__(1024) prefill_plan_kernel(
     const int off = base_pg + block_excl_scan(np, warp_sum, &tot_pg);
     if (isdec) {
       mo.rows[d] = cu_q[s];
-#pragma unroll
-      for (int k = 0; k < 8; ++k) mo.counters[size_t(d) * 8 + k] = 0;
+      mo.counters[d] = 0;
       for (int p = 0; p < np; ++p) {
         const int id = mo.kv_indices[pa + p];
         if (id < 0 || id >= mo.num_blocks) flag(st, PKV_DEV_SLOT_OOB);
