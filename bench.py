@@ -925,6 +925,26 @@ def run_swap(torch, bk, args, device, tables, ctx, qs, ks, vs) -> dict:
     sw = B200SwapSpace(bk, staging_bytes=256 << 20, synchronous=False)
     per_dir = victims * sw.bytes_for(nbv)
 
+    # host-link peak: one contiguous 1 GiB pinned <-> device copy per direction
+    # (cudaMemcpyAsync on a side stream, CUDA events, best of 5)
+    link = {}
+    hbuf = torch.empty(1 << 30, dtype=torch.uint8).pin_memory()
+    dbuf = torch.empty(1 << 30, dtype=torch.uint8, device=device)
+    ls = torch.cuda.Stream(device=device)
+    for name, dst_t, src_t in (("d2h", hbuf, dbuf), ("h2d", dbuf, hbuf)):
+        best = None
+        for _ in range(6):
+            a_, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with torch.cuda.stream(ls):
+                a_.record(ls)
+                dst_t.copy_(src_t, non_blocking=True)
+                b_.record(ls)
+            ls.synchronize()
+            t = a_.elapsed_time(b_)
+            best = t if best is None else min(best, t)
+        link[name] = round((1 << 30) / (best / 1e3) / 1e9, 2)
+    del hbuf, dbuf
+
     # the concurrent decode: first 128 sequences of the config-2 batch, one step
     nd = 128
     m = build_meta([t for t in tables[:nd]], ctx[:nd], [1] * nd, P, device=device)
@@ -952,7 +972,7 @@ def run_swap(torch, bk, args, device, tables, ctx, qs, ks, vs) -> dict:
     torch.cuda.synchronize()
     alone_ms = e0.elapsed_time(e1) / reps
 
-    def once(with_decode):
+    def once(with_decode, sw=sw):
         torch.cuda.synchronize()
         steps = {"out": 0, "in": 0}
 
@@ -1002,16 +1022,37 @@ def run_swap(torch, bk, args, device, tables, ctx, qs, ks, vs) -> dict:
         ok = ok and bool(torch.equal(bk._pool[:, :, src[i]], bk._pool[:, :, dst[i]]))
     for h in hs:
         sw.release(h)
+    # the same with staging that holds the whole swap: no gather waits for an
+    # earlier victim's host copy, so the compute stream waits only for gathers
+    big = B200SwapSpace(bk, staging_bytes=int(per_dir), synchronous=False)
+    hs, to3, ti3, dec_out3, dec_in3, steps3 = once(True, big)
+    for i in range(0, victims, 9):
+        ok = ok and bool(torch.equal(bk._pool[:, :, src[i]], bk._pool[:, :, dst[i]]))
+    for h in hs:
+        big.release(h)
+    del big
     bk.check_status()
     del gr
     return {"victims": victims, "tokens": toks, "bytes_per_direction": int(per_dir),
             "d2h_gbs": round(per_dir / t_out / 1e9, 2), "h2d_gbs": round(per_dir / t_in / 1e9, 2),
+            "link_peak_gbs": link,
+            "frac_of_link": {"d2h": round(per_dir / t_out / 1e9 / link["d2h"], 4),
+                             "h2d": round(per_dir / t_in / 1e9 / link["h2d"], 4)},
+            "link_probe": "contiguous 1 GiB pinned host <-> device cudaMemcpyAsync, best of 6, CUDA events",
             "bit_exact_spot_check": ok, "timing": "host wall clock around issue + wait",
             "overlapped": {"d2h_gbs": round(per_dir / to2 / 1e9, 2), "h2d_gbs": round(per_dir / ti2 / 1e9, 2),
                            "decode_batch": nd, "decode_ms_per_step_alone": round(alone_ms, 4),
                            "decode_ms_per_step_during_swap_out": round(dec_out, 4) if dec_out else None,
                            "decode_ms_per_step_during_swap_in": round(dec_in, 4) if dec_in else None,
-                           "decode_steps_during": steps}}
+                           "decode_steps_during": steps, "staging_bytes": 256 << 20,
+                           "why": ("a swap-out makes the compute stream wait until its blocks were read; with "
+                                   "staging smaller than the swap each gather first waits for an earlier "
+                                   "victim's host copy, so the decode steps follow the host link")},
+            "overlapped_whole_swap_staged": {
+                "d2h_gbs": round(per_dir / to3 / 1e9, 2), "h2d_gbs": round(per_dir / ti3 / 1e9, 2),
+                "decode_ms_per_step_during_swap_out": round(dec_out3, 4) if dec_out3 else None,
+                "decode_ms_per_step_during_swap_in": round(dec_in3, 4) if dec_in3 else None,
+                "decode_steps_during": steps3, "staging_bytes": int(per_dir)}}
 
 
 def run_llama(torch, bk, args, device, rank) -> dict:

@@ -4,7 +4,9 @@
 //
 // All of these are HBM-bound byte copies: the kernels move 16-byte vectors
 // with coalesced loads and stores and never reshape the work into GEMMs.
+#include <deque>
 #include <map>
+#include <vector>
 #include <string>
 
 #include "pkv_common.cuh"
@@ -293,17 +295,31 @@ extern "C" int pkv_swap_scatter(const pkv_pool* pool, const int32_t* block_ids, 
 
 // ------------------------------------------------------------------ swap engine
 
+// Staging is a ring: each chunk of a transfer takes the next contiguous region
+// (wrapping to the start when the tail is too short) and waits, on the stream
+// that writes it, only for the earlier uses it overlaps. A use ends at an event
+// recorded after the last operation that reads or writes the region (the D2H
+// copy of a swap-out, the scatter kernel of a swap-in); ended uses are pruned
+// by querying their events. So transfers smaller than the staging area do not
+// wait for one another, and the gather of a swap-out (which the compute stream
+// waits for) waits for a host copy only once the staging area is full.
+struct StageUse {
+  size_t off, len;
+  cudaEvent_t done;
+};
+
 struct pkv_swapper {
   int device = 0;
   char* staging = nullptr;
-  size_t half_bytes = 0;
+  size_t staging_bytes = 0;
+  size_t chunk_bytes = 0;          // largest region one chunk takes (half the ring)
+  size_t head = 0;                 // next free offset of the ring
+  std::deque<StageUse> uses;       // regions in use, oldest first
+  std::vector<cudaEvent_t> spare;  // events of ended uses, for reuse
   cudaStream_t kstream = nullptr;  // gather / scatter kernels
   cudaStream_t cstream = nullptr;  // copy-engine transfers
-  cudaEvent_t ready[2] = {nullptr, nullptr};
-  cudaEvent_t last_use[2] = {nullptr, nullptr};
-  bool used[2] = {false, false};
+  cudaEvent_t ready = nullptr;     // a chunk's first stage done (gathered, resp. copied in)
   cudaEvent_t ev_start = nullptr, ev_kdone = nullptr;
-  int cur = 0;
   uint64_t next_ticket = 1;
   std::map<uint64_t, cudaEvent_t> tickets;
 };
@@ -318,6 +334,39 @@ int check_swapper(pkv_swapper* sw) {
   if (dev != sw->device)
     return fail(PKV_ERR_ARG, "swapper used on device " + std::to_string(dev) + " but created on " +
                                  std::to_string(sw->device));
+  return PKV_OK;
+}
+
+// A region of `len` bytes (<= chunk_bytes) for a chunk written on `writer`:
+// `writer` waits for every earlier use the region overlaps.
+int stage_alloc(pkv_swapper* sw, size_t len, cudaStream_t writer, size_t* off) {
+  while (!sw->uses.empty()) {  // prune the uses that ended
+    const cudaError_t q = cudaEventQuery(sw->uses.front().done);
+    if (q == cudaErrorNotReady) break;
+    if (q != cudaSuccess) return cuda_fail(q, "cudaEventQuery");
+    sw->spare.push_back(sw->uses.front().done);
+    sw->uses.pop_front();
+  }
+  size_t o = sw->head;
+  if (o + len > sw->staging_bytes) o = 0;
+  for (const StageUse& u : sw->uses)
+    if (u.off < o + len && o < u.off + u.len) PKV_CUDA_RET(cudaStreamWaitEvent(writer, u.done, 0));
+  sw->head = o + len;
+  *off = o;
+  return PKV_OK;
+}
+
+// The region [off, off + len) is in use until the work queued on `last` so far.
+int stage_release(pkv_swapper* sw, size_t off, size_t len, cudaStream_t last) {
+  cudaEvent_t e;
+  if (!sw->spare.empty()) {
+    e = sw->spare.back();
+    sw->spare.pop_back();
+  } else {
+    PKV_CUDA_RET(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+  }
+  PKV_CUDA_RET(cudaEventRecord(e, last));
+  sw->uses.push_back({off, len, e});
   return PKV_OK;
 }
 
@@ -346,14 +395,12 @@ extern "C" int pkv_swapper_create(void* staging, size_t staging_bytes, pkv_swapp
   if (reinterpret_cast<uintptr_t>(staging) % 16) return fail(PKV_ERR_ARG, "staging must be 16-byte aligned");
   pkv_swapper* sw = new pkv_swapper();
   sw->staging = static_cast<char*>(staging);
-  sw->half_bytes = (staging_bytes / 2) & ~size_t(15);
+  sw->staging_bytes = staging_bytes & ~size_t(15);
+  sw->chunk_bytes = (staging_bytes / 2) & ~size_t(15);
   cudaError_t e = cudaGetDevice(&sw->device);
   if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&sw->kstream, cudaStreamNonBlocking);
   if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&sw->cstream, cudaStreamNonBlocking);
-  for (int i = 0; i < 2 && e == cudaSuccess; ++i) {
-    e = cudaEventCreateWithFlags(&sw->ready[i], cudaEventDisableTiming);
-    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&sw->last_use[i], cudaEventDisableTiming);
-  }
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&sw->ready, cudaEventDisableTiming);
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&sw->ev_start, cudaEventDisableTiming);
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&sw->ev_kdone, cudaEventDisableTiming);
   if (e != cudaSuccess) {
@@ -369,10 +416,9 @@ extern "C" int pkv_swapper_destroy(pkv_swapper* sw) {
   if (sw->kstream) cudaStreamSynchronize(sw->kstream);
   if (sw->cstream) cudaStreamSynchronize(sw->cstream);
   for (auto& kv : sw->tickets) cudaEventDestroy(kv.second);
-  for (int i = 0; i < 2; ++i) {
-    if (sw->ready[i]) cudaEventDestroy(sw->ready[i]);
-    if (sw->last_use[i]) cudaEventDestroy(sw->last_use[i]);
-  }
+  for (auto& u : sw->uses) cudaEventDestroy(u.done);
+  for (auto ev : sw->spare) cudaEventDestroy(ev);
+  if (sw->ready) cudaEventDestroy(sw->ready);
   if (sw->ev_start) cudaEventDestroy(sw->ev_start);
   if (sw->ev_kdone) cudaEventDestroy(sw->ev_kdone);
   if (sw->kstream) cudaStreamDestroy(sw->kstream);
@@ -392,7 +438,7 @@ extern "C" int pkv_swap_out(pkv_swapper* sw, const pkv_pool* pool, const int32_t
   if (!block_ids || !host_k || !host_v) return fail(PKV_ERR_ARG, "block_ids and host buffers must be non-NULL");
   const pkv_pool& p = *pool;
   const int64_t bb = block_bytes(p);
-  const int64_t chunk = int64_t(sw->half_bytes) / bb;
+  const int64_t chunk = int64_t(sw->chunk_bytes) / bb;
   if (chunk < 1) return fail(PKV_ERR_ARG, "staging half smaller than one block");
   const int64_t per_kv = int64_t(p.num_layers) * nb, segs = 2 * per_kv;
   char* hk = static_cast<char*>(host_k);
@@ -403,14 +449,13 @@ extern "C" int pkv_swap_out(pkv_swapper* sw, const pkv_pool* pool, const int32_t
   PKV_CUDA_RET(cudaStreamWaitEvent(sw->kstream, sw->ev_start, 0));
   for (int64_t j0 = 0; j0 < segs; j0 += chunk) {
     const int64_t cnt = std::min(chunk, segs - j0);
-    const int h = sw->cur;
-    sw->cur ^= 1;
-    char* stage = sw->staging + h * sw->half_bytes;
-    if (sw->used[h]) PKV_CUDA_RET(cudaStreamWaitEvent(sw->kstream, sw->last_use[h], 0));
+    size_t off = 0;
+    if (int rc = stage_alloc(sw, size_t(cnt * bb), sw->kstream, &off)) return rc;
+    char* stage = sw->staging + off;
     if (int rc = launch_swap<true>(p, block_ids, nb, stage, j0, cnt, dev_status, sw->kstream))
       return rc;
-    PKV_CUDA_RET(cudaEventRecord(sw->ready[h], sw->kstream));
-    PKV_CUDA_RET(cudaStreamWaitEvent(sw->cstream, sw->ready[h], 0));
+    PKV_CUDA_RET(cudaEventRecord(sw->ready, sw->kstream));
+    PKV_CUDA_RET(cudaStreamWaitEvent(sw->cstream, sw->ready, 0));
     // the chunk is contiguous in the host layout except where it crosses K -> V
     int64_t j = j0;
     while (j < j0 + cnt) {
@@ -419,8 +464,7 @@ extern "C" int pkv_swap_out(pkv_swapper* sw, const pkv_pool* pool, const int32_t
                                    size_t((end - j) * bb), cudaMemcpyDeviceToHost, sw->cstream));
       j = end;
     }
-    PKV_CUDA_RET(cudaEventRecord(sw->last_use[h], sw->cstream));
-    sw->used[h] = true;
+    if (int rc = stage_release(sw, off, size_t(cnt * bb), sw->cstream)) return rc;
   }
   // later compute-stream work (writes into the freed blocks) waits for the reads only
   PKV_CUDA_RET(cudaEventRecord(sw->ev_kdone, sw->kstream));
@@ -439,7 +483,7 @@ extern "C" int pkv_swap_in(pkv_swapper* sw, const pkv_pool* pool, const int32_t*
   if (!block_ids || !host_k || !host_v) return fail(PKV_ERR_ARG, "block_ids and host buffers must be non-NULL");
   const pkv_pool& p = *pool;
   const int64_t bb = block_bytes(p);
-  const int64_t chunk = int64_t(sw->half_bytes) / bb;
+  const int64_t chunk = int64_t(sw->chunk_bytes) / bb;
   if (chunk < 1) return fail(PKV_ERR_ARG, "staging half smaller than one block");
   const int64_t per_kv = int64_t(p.num_layers) * nb, segs = 2 * per_kv;
   char* hk = const_cast<char*>(static_cast<const char*>(host_k));
@@ -450,10 +494,9 @@ extern "C" int pkv_swap_in(pkv_swapper* sw, const pkv_pool* pool, const int32_t*
   PKV_CUDA_RET(cudaStreamWaitEvent(sw->kstream, sw->ev_start, 0));
   for (int64_t j0 = 0; j0 < segs; j0 += chunk) {
     const int64_t cnt = std::min(chunk, segs - j0);
-    const int h = sw->cur;
-    sw->cur ^= 1;
-    char* stage = sw->staging + h * sw->half_bytes;
-    if (sw->used[h]) PKV_CUDA_RET(cudaStreamWaitEvent(sw->cstream, sw->last_use[h], 0));
+    size_t off = 0;
+    if (int rc = stage_alloc(sw, size_t(cnt * bb), sw->cstream, &off)) return rc;
+    char* stage = sw->staging + off;
     int64_t j = j0;
     while (j < j0 + cnt) {
       const int64_t end = (j < per_kv) ? std::min(j0 + cnt, per_kv) : j0 + cnt;
@@ -461,12 +504,11 @@ extern "C" int pkv_swap_in(pkv_swapper* sw, const pkv_pool* pool, const int32_t*
                                    size_t((end - j) * bb), cudaMemcpyHostToDevice, sw->cstream));
       j = end;
     }
-    PKV_CUDA_RET(cudaEventRecord(sw->ready[h], sw->cstream));
-    PKV_CUDA_RET(cudaStreamWaitEvent(sw->kstream, sw->ready[h], 0));
+    PKV_CUDA_RET(cudaEventRecord(sw->ready, sw->cstream));
+    PKV_CUDA_RET(cudaStreamWaitEvent(sw->kstream, sw->ready, 0));
     if (int rc = launch_swap<false>(p, block_ids, nb, stage, j0, cnt, dev_status, sw->kstream))
       return rc;
-    PKV_CUDA_RET(cudaEventRecord(sw->last_use[h], sw->kstream));
-    sw->used[h] = true;
+    if (int rc = stage_release(sw, off, size_t(cnt * bb), sw->kstream)) return rc;
   }
   PKV_CUDA_RET(cudaEventRecord(sw->ev_kdone, sw->kstream));
   PKV_CUDA_RET(cudaStreamWaitEvent(cs, sw->ev_kdone, 0));
