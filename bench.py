@@ -1209,6 +1209,56 @@ def run_llama(torch, bk, args, device, rank) -> dict:
             "timing": "host wall clock around the steps (host scheduling, batch assembly, H2D, forward, D2H)"}
 
 
+def kvops_probe() -> None:
+    """A small fixed workload of the KV-append, copy-on-write and swap kernels
+    for kernel profilers (ncu): on a 16-layer, 8000-block (4 GB) pool,
+    append_kv of 256 scattered slots per layer (config 2's step) 3 x 16 times,
+    copy_blocks of 420 pairs (config 3's copy-on-write count) 3 times, and
+    swap_out + swap_in of 8 victims x 64 blocks twice. Prints one JSON line."""
+    import torch
+
+    from llm_serving_layer_b200 import B200PagedBackend, B200SwapSpace
+    from llm_serving_layer_b200.meta import BatchMeta
+
+    dev = torch.device("cuda", 0)
+    nb = 8000
+    bk = B200PagedBackend(L, nb, P, HKV, HQ, D, device=dev, dtype=torch.float16, validate="device")
+    rs = np.random.RandomState(0)
+    perm = rs.permutation(nb)
+    slots = torch.as_tensor(perm[:256] * P + rs.randint(0, P, 256), dtype=torch.int32, device=dev)
+    z = torch.zeros(1, dtype=torch.int32, device=dev)
+    m = BatchMeta(query_lens=z, cu_query_lens=torch.zeros(2, dtype=torch.int32, device=dev), kv_lens=z,
+                  positions=torch.zeros(256, dtype=torch.int64, device=dev), last_token_ix=z,
+                  kv_indptr=torch.zeros(2, dtype=torch.int32, device=dev),
+                  kv_indices=torch.zeros(0, dtype=torch.int32, device=dev), kv_last_page_len=z,
+                  batch_indices=torch.zeros(256, dtype=torch.int32, device=dev), slot_mapping=slots)
+    k = torch.randn(256, HKV, D, device=dev).half()
+    v = torch.randn(256, HKV, D, device=dev).half()
+    for _ in range(3):
+        for layer in range(L):
+            bk.append_kv(layer, k, v, m)
+    src, dst = perm[256:676].tolist(), perm[676:1096].tolist()
+    for _ in range(3):
+        bk.copy_blocks(src, dst)
+    sw = B200SwapSpace(bk, staging_bytes=512 << 20, synchronous=True)
+
+    class Blocks:
+        def __init__(self, ids, n):
+            self.block_ids, self.num_tokens, self.seq_id, self.is_freed = list(ids), n, 0, False
+
+    vic = [perm[1100 + 64 * i:1164 + 64 * i].tolist() for i in range(8)]
+    new = [perm[1700 + 64 * i:1764 + 64 * i].tolist() for i in range(8)]
+    for _ in range(2):
+        hs = [sw.swap_out(f"v{i}", Blocks(vic[i], 1024)) for i in range(8)]
+        for i in range(8):
+            sw.swap_in(hs[i], Blocks(new[i], 1024))
+        for h in hs:
+            sw.release(h)
+    torch.cuda.synchronize()
+    bk.check_status()
+    print(json.dumps({"kvops_probe": "ok", "appends": 3 * L, "copy_blocks_launches": 3, "swaps": 16}))
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -1228,7 +1278,12 @@ def main() -> None:
                          "the reference API, with the fused step reported beside it)")
     ap.add_argument("--no-fused-extra", dest="fused_extra", action="store_false")
     ap.add_argument("--llama-steps", type=int, default=100)
+    ap.add_argument("--kvops-probe", action="store_true",
+                    help="run only the small append / copy-on-write / swap workload (for kernel profilers)")
     args = ap.parse_args()
+    if args.kvops_probe:
+        kvops_probe()
+        return
     args.warmup = max(3, args.warmup)
     if args.impl == "reference":
         args.steps_ref = max(1, min(args.steps, 100))
