@@ -487,6 +487,8 @@ def run_b200(args) -> None:
     e2e = run_e2e(torch, bk, tables, ctx, args, device, ws, dist, n_graphs, "device")
     host_e2e = run_e2e(torch, bk, tables, ctx, args, device, ws, dist, n_graphs, "host")
     e2e["host_meta"] = {k: host_e2e[k] for k in ("value", "ms_per_step", "h2d_bytes_per_step", "path")}
+    fused_e2e = run_e2e(torch, bk, tables, ctx, args, device, ws, dist, n_graphs, "device", fused=True)
+    e2e["fused"] = {k: fused_e2e[k] for k in ("value", "ms_per_step", "path")}
 
     line_extra = {}
     # ---- swap (config 4), rank 0 measures its own GPU's host link
@@ -546,18 +548,24 @@ def run_b200(args) -> None:
         dist.destroy_process_group()
 
 
-def run_e2e(torch, bk, tables, ctx, args, device, ws, dist, n_graphs, meta_mode="device") -> dict:
+def run_e2e(torch, bk, tables, ctx, args, device, ws, dist, n_graphs, meta_mode="device",
+            fused=False) -> dict:
     """Public-API end to end: per step, the step's BatchMeta (``meta_mode``
     "device": DeviceBlockTables.build_batch_meta, the rows' lengths plus the
     blocks of rows that crossed into a new page copied in one pinned transfer
     and every field computed on the GPU; "host": build_meta on the host and one
-    copy per field), the step's q/k/v for 16 layers copied from pinned host
-    memory (one buffer per layer), append_kv + attend per layer (the reference
-    engine's calls), every layer's attention output copied back to pinned host
-    memory, one synchronize. The copies run on a side stream, ordered by
-    events: layer l waits only for its own inputs, and its output leaves as
-    soon as layer l finished; the next step's meta is built on the host while
-    this step's GPU work runs. Timed with CUDA events around the whole loop."""
+    copy per field), the step's q/k/v for 16 layers copied from one pinned host
+    buffer, append_kv + attend per layer (the reference engine's calls; with
+    ``fused``, append_attend), the attention outputs copied back to pinned host
+    memory, one synchronize. The copies run on two side streams (inputs and
+    outputs, so both directions of the link run at once), ordered by events:
+    the inputs of step s + 1 (all layers, one copy) go into a second device
+    buffer while step s computes, and the outputs (written by attend into one
+    buffer, out=) leave four layers at a time as soon as those layers finished.
+    The next step's meta is built and planned on the host while this step's GPU
+    work runs. Every step's inputs and outputs cross the link inside the timed
+    region (the first timed step also copies its own). Timed with CUDA events
+    around the whole loop."""
     from llm_serving_layer_b200 import DeviceBlockTables
     from llm_serving_layer_b200.meta import build_meta
 
@@ -565,18 +573,27 @@ def run_e2e(torch, bk, tables, ctx, args, device, ws, dist, n_graphs, meta_mode=
     base = args.warmup  # fresh lengths continue from the graph steps' start
     rs = np.random.RandomState(args.seed + 7)
     nq, nk = N_SEQ * HQ * D, N_SEQ * HKV * D
-    hx = []
-    for _ in range(L):  # one pinned buffer per layer: q | k | v
-        x = np.concatenate([rs.standard_normal(nq), rs.standard_normal(2 * nk) * KV_STD]).astype(np.float16)
-        hx.append(torch.from_numpy(x).pin_memory())
-    hout = [torch.empty((N_SEQ, HQ, D), dtype=torch.float16).pin_memory() for _ in range(L)]
-    dx = [torch.empty_like(x, device=device) for x in hx]
-    dq = [x[:nq].view(N_SEQ, HQ, D) for x in dx]
-    dk = [x[nq:nq + nk].view(N_SEQ, HKV, D) for x in dx]
-    dv = [x[nq + nk:].view(N_SEQ, HKV, D) for x in dx]
+    per = nq + 2 * nk
+    # all layers' inputs in one pinned buffer (layer l: q | k | v), one copy per step
+    hx = torch.from_numpy(np.concatenate([
+        np.concatenate([rs.standard_normal(nq), rs.standard_normal(2 * nk) * KV_STD]) for _ in range(L)
+    ]).astype(np.float16)).pin_memory()
+    # all layers' outputs in one device buffer and one pinned buffer, copied back in groups of layers
+    GROUP = 4
+    dout = torch.empty((L, N_SEQ, HQ, D), dtype=torch.float16, device=device)
+    hout = torch.empty((L, N_SEQ, HQ, D), dtype=torch.float16).pin_memory()
+    # two device copies of the inputs: step s + 1's are copied in while step s runs
+    dx = [torch.empty_like(hx, device=device) for _ in range(2)]
+    dq = [[b[l * per:l * per + nq].view(N_SEQ, HQ, D) for l in range(L)] for b in dx]
+    dk = [[b[l * per + nq:l * per + nq + nk].view(N_SEQ, HKV, D) for l in range(L)] for b in dx]
+    dv = [[b[l * per + nq + nk:(l + 1) * per].view(N_SEQ, HKV, D) for l in range(L)] for b in dx]
     comp = torch.cuda.current_stream(device)
-    cstream = torch.cuda.Stream(device=device)
-    ev_in = [torch.cuda.Event() for _ in range(L)]
+    cstream = torch.cuda.Stream(device=device)  # host -> device inputs
+    ostream = torch.cuda.Stream(device=device)  # device -> host outputs (the other direction of the link)
+    ev_ready = [torch.cuda.Event(), torch.cuda.Event()]  # buffer b holds its step's inputs
+    ev_free = [torch.cuda.Event(), torch.cuda.Event()]   # buffer b is no longer read
+    for e in ev_free:
+        e.record(comp)
     ev_out = [torch.cuda.Event() for _ in range(L)]
     rows = np.arange(N_SEQ, dtype=np.int32)
     ones = np.ones(N_SEQ, dtype=np.int64)
@@ -599,27 +616,46 @@ def run_e2e(torch, bk, tables, ctx, args, device, ws, dist, n_graphs, meta_mode=
         return m
 
     nxt = {}
+    staged = set()  # steps whose inputs were copied in
+
+    def h2d(step):
+        b = step % 2
+        cstream.wait_event(ev_free[b])
+        with torch.cuda.stream(cstream):
+            dx[b].copy_(hx, non_blocking=True)
+            ev_ready[b].record(cstream)
+        staged.add(step)
 
     def one(s):
         # step s runs with the meta built during step s - 1; the next step's meta
         # is built on the host while this step's GPU work runs (one build per step)
         m = nxt.pop(s) if s in nxt else meta_for_step(s)
-        cstream.wait_stream(comp)  # the previous step is done with the device buffers
-        with torch.cuda.stream(cstream):
-            for layer in range(L):
-                dx[layer].copy_(hx[layer], non_blocking=True)
-                ev_in[layer].record(cstream)
-        outs = []
+        if s not in staged:
+            h2d(s)
+        h2d(s + 1)  # the next step's inputs travel while this step computes
+        staged.discard(s)
+        b = s % 2
+        comp.wait_event(ev_ready[b])
         for layer in range(L):
-            comp.wait_event(ev_in[layer])
-            bk.append_kv(layer, dk[layer], dv[layer], m)
-            outs.append(bk.attend(dq[layer], layer, SCALE, m))
-            ev_out[layer].record(comp)
-            cstream.wait_event(ev_out[layer])
-            with torch.cuda.stream(cstream):
-                hout[layer].copy_(outs[layer], non_blocking=True)
+            if fused:
+                bk.append_attend(layer, dk[b][layer], dv[b][layer], dq[b][layer], SCALE, m, out=dout[layer])
+            else:
+                bk.append_kv(layer, dk[b][layer], dv[b][layer], m)
+                bk.attend(dq[b][layer], layer, SCALE, m, out=dout[layer])
+            if layer % GROUP == GROUP - 1:
+                ev_out[layer].record(comp)
+        ev_free[b].record(comp)
+        # each group of layers' outputs leaves as soon as the group is done (the
+        # output stream waits for its event); issued together to switch streams once
+        with torch.cuda.stream(ostream):
+            for g0 in range(0, L, GROUP):
+                ostream.wait_event(ev_out[g0 + GROUP - 1])
+                hout[g0:g0 + GROUP].copy_(dout[g0:g0 + GROUP], non_blocking=True)
         nxt[s + 1] = meta_for_step(s + 1)
-        cstream.synchronize()
+        # plan the next step now (B200PagedBackend.plan): its host work and plan
+        # kernel run while this step's GPU work drains, not before its first layer
+        bk.plan(nxt[s + 1])
+        ostream.synchronize()
 
     if meta_mode == "device":  # admission: each row gets the blocks of its history
         for r in range(N_SEQ):
@@ -627,6 +663,8 @@ def run_e2e(torch, bk, tables, ctx, args, device, ws, dist, n_graphs, meta_mode=
     for s in range(3):
         one(s)
     nxt.clear()
+    staged.clear()
+    torch.cuda.synchronize()
     nxt[0] = meta_for_step(0)
     meta_in.update(bytes=0, n=0)
     if ws > 1:
@@ -640,14 +678,17 @@ def run_e2e(torch, bk, tables, ctx, args, device, ws, dist, n_graphs, meta_mode=
     torch.cuda.synchronize()
     ms = max_over_ranks(dist, e0.elapsed_time(e1), device)
     bk.check_status()
-    h2d = L * hx[0].numel() * 2 + meta_in["bytes"] // max(meta_in["n"], 1)
-    d2h = L * hout[0].numel() * 2
-    path = ("B200PagedBackend.append_kv/attend per layer, validate='device', "
+    h2d_bytes = hx.numel() * 2 + meta_in["bytes"] // max(meta_in["n"], 1)
+    d2h = hout.numel() * 2
+    path = (("B200PagedBackend.append_attend per layer" if fused else "B200PagedBackend.append_kv/attend per layer")
+            + ", validate='device', "
             + ("DeviceBlockTables.build_batch_meta (BatchMeta fields computed on the GPU from device block "
                "tables; only new blocks travel)" if meta_mode == "device" else
                "host build_meta (one copy per BatchMeta field)")
-            + " built per step (the next step's while this one runs), copies on a side stream")
-    return {"value": round(N_SEQ * ws * steps / (ms / 1e3), 1), "unit": UNIT, "h2d_bytes_per_step": int(h2d),
+            + " built per step (the next step's while this one runs), inputs one copy per step (one step "
+              "ahead, double-buffered), outputs into one buffer (attend out=) copied back 4 layers at a time, "
+              "on two side streams")
+    return {"value": round(N_SEQ * ws * steps / (ms / 1e3), 1), "unit": UNIT, "h2d_bytes_per_step": int(h2d_bytes),
             "d2h_bytes_per_step": int(d2h), "steps": steps, "ms_per_step": round(ms / steps, 4), "path": path}
 
 

@@ -138,5 +138,17 @@ def stream_ptr(device: torch.device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
+def raw_stream(device_index: int) -> int:
+    """cudaStream_t of torch's current stream on `device_index` (the handle
+    torch.cuda.current_stream(device).cuda_stream returns, without building a
+    Stream object on every call)."""
+    if _raw_stream is not None:
+        return _raw_stream(device_index)
+    return torch.cuda.current_stream(device_index).cuda_stream
+
+
 def ptr(t: torch.Tensor | None) -> int | None:
     return None if t is None else t.data_ptr()

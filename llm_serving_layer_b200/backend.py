@@ -185,10 +185,10 @@ class B200PagedBackend:
             return
         N.check(self._lib.pkv_append_kv(self._pdesc, layer_idx, k.data_ptr(), v.data_ptr(),
                                         slots.data_ptr(), tokens, self._status_ptr,
-                                        torch.cuda.current_stream(self.device).cuda_stream), "append_kv")
+                                        N.raw_stream(self._dev_index)), "append_kv")
 
     def append_attend(self, layer_idx: int, k: torch.Tensor, v: torch.Tensor, q: torch.Tensor,
-                      scale: float, meta: Any) -> torch.Tensor:
+                      scale: float, meta: Any, *, out: torch.Tensor | None = None) -> torch.Tensor:
         """``append_kv(layer_idx, k, v, meta)`` then ``attend(q, layer_idx, scale,
         meta)`` in one call, with the same checks, errors and results. A decode
         step is ONE kernel launch: the decode kernel writes each sequence's new
@@ -203,7 +203,7 @@ class B200PagedBackend:
         if st["n_tokens"] != tokens:
             raise ValueError(f"meta describes {st['n_tokens']} tokens but q has {tokens}")
         q = self._own(q, self.dtype)
-        out = torch.empty_like(q)
+        out = self._out(q, out)
         if tokens == 0:
             return out
         self.n_runs += 1
@@ -211,7 +211,7 @@ class B200PagedBackend:
         N.check(self._lib.pkv_append_attend_planned(
             self._pdesc, layer_idx, self.n_heads, k.data_ptr(), v.data_ptr(), slots.data_ptr(), q.data_ptr(),
             out.data_ptr(), float(scale), st["batch_ref"], st["hint"], st["ws_ptr"], st["ws_bytes"],
-            torch.cuda.current_stream(self.device).cuda_stream), "append_attend")
+            N.raw_stream(self._dev_index)), "append_attend")
         return out
 
     def _append_args(self, layer_idx: int, k: torch.Tensor, v: torch.Tensor, meta: Any):
@@ -243,11 +243,15 @@ class B200PagedBackend:
 
     # -- read path -------------------------------------------------------------
 
-    def attend(self, q: torch.Tensor, layer_idx: int, scale: float, meta: Any) -> torch.Tensor:
+    def attend(self, q: torch.Tensor, layer_idx: int, scale: float, meta: Any, *,
+               out: torch.Tensor | None = None) -> torch.Tensor:
         """Attention over each sequence's full KV history including this step's
         append (``paged_torch.py:280-485``): GQA ``h // groups``, bottom-right
         causal mask, pages read in listed order, the unwritten tail of the last
-        page never read. Returns ``(tokens, n_heads, head_dim)`` in the pool dtype."""
+        page never read. Returns ``(tokens, n_heads, head_dim)`` in the pool dtype:
+        a new tensor, or ``out`` (an optional extension of the reference's
+        signature: a contiguous tensor of that shape and dtype on this device,
+        written in place)."""
         self._check_layer(layer_idx)
         tokens = q.shape[0]
         if q.shape != (tokens, self.n_heads, self.head_dim):
@@ -258,7 +262,7 @@ class B200PagedBackend:
         if st["n_tokens"] != tokens:
             raise ValueError(f"meta describes {st['n_tokens']} tokens but q has {tokens}")
         q = self._own(q, self.dtype)
-        out = torch.empty_like(q)
+        out = self._out(q, out)
         if tokens == 0:
             return out
         self.n_runs += 1
@@ -266,7 +270,7 @@ class B200PagedBackend:
         N.check(self._lib.pkv_attend_planned(
             self._pdesc, layer_idx, self.n_heads, q.data_ptr(), out.data_ptr(), float(scale),
             st["batch_ref"], st["hint"], st["ws_ptr"], st["ws_bytes"],
-            torch.cuda.current_stream(self.device).cuda_stream), "attend")
+            N.raw_stream(self._dev_index)), "attend")
         return out
 
     # -- per-step plan -----------------------------------------------------------
@@ -411,6 +415,17 @@ class B200PagedBackend:
 
     def _i32(self, t: torch.Tensor) -> torch.Tensor:
         return t.to(device=self.device, dtype=torch.int32).contiguous()
+
+    def _out(self, q: torch.Tensor, out: torch.Tensor | None) -> torch.Tensor:
+        if out is None:
+            return torch.empty_like(q)
+        if (out.shape != q.shape or out.dtype != self.dtype or not out.is_cuda
+                or out.get_device() != self._dev_index or not out.is_contiguous()):
+            raise ValueError(f"out must be a contiguous {tuple(q.shape)} {self.dtype} tensor on {self.device}")
+        nb = q.numel() * q.element_size()
+        if out.data_ptr() < q.data_ptr() + nb and q.data_ptr() < out.data_ptr() + nb:
+            raise ValueError("out must not overlap q (other CTAs may still read a row being written)")
+        return out
 
     def _own(self, t: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
         """t on this device in `dtype`, contiguous (no op when it already is)."""

@@ -69,6 +69,7 @@ class _Slot:
     def resize_input(self, device: torch.device, words: int) -> None:
         self.host = torch.empty(words, dtype=torch.int32).pin_memory()
         self.host_np = self.host.numpy()
+        self.host_ptr = self.host.data_ptr()
         self.dev = torch.empty(words, dtype=torch.int32, device=device)
 
 
@@ -95,6 +96,7 @@ class DeviceBlockTables:
             raise ValueError(f"DeviceBlockTables requires a CUDA device, got {self.device}; it has no CPU path")
         if self.device.index is None:
             self.device = torch.device("cuda", torch.cuda.current_device())
+        self._dev_index = self.device.index
         self._lib = N.lib()
         self.max_seqs, self.max_pages, self.block_size = int(max_seqs), int(max_pages), int(block_size)
         self.num_blocks = int(num_blocks)
@@ -153,17 +155,38 @@ class DeviceBlockTables:
         pages, the missing pages from the host-side ``block_tables[i]`` (the
         allocator's lists, sequence i = rows[i]). Returns the pages recorded."""
         rows = np.asarray(rows, dtype=np.int64)
-        need = (np.asarray(kv_lens, dtype=np.int64) + self.block_size - 1) // self.block_size
-        short = np.nonzero(need > self.pages[rows])[0]
-        added = 0
-        for i in short.tolist():
-            r, have, want = int(rows[i]), int(self.pages[rows[i]]), int(need[i])
-            if len(block_tables[i]) < want:
-                raise ValueError(f"seq {i}: {len(block_tables[i])} blocks hold fewer than kv_len="
-                                 f"{int(np.asarray(kv_lens)[i])} tokens")
-            self.extend(r, block_tables[i][have:want])
-            added += want - have
-        return added
+        kv = np.asarray(kv_lens, dtype=np.int64)
+        if rows.size and (int(rows.min()) < 0 or int(rows.max()) >= self.max_seqs):
+            raise IndexError(f"rows outside [0, {self.max_seqs})")
+        need = (kv + self.block_size - 1) // self.block_size
+        have = self.pages[rows]
+        short = np.nonzero(need > have)[0]
+        if not short.size:
+            return 0
+        if int(need[short].max()) > self.max_pages:
+            i = int(short[np.argmax(need[short])])
+            raise ValueError(f"row {int(rows[i])}: {int(need[i])} pages exceed max_pages={self.max_pages}")
+        ids: list[int] = []
+        for i in short.tolist():  # the new blocks of every growing row, in row order
+            t, h, w = block_tables[i], int(have[i]), int(need[i])
+            if len(t) < w:
+                raise ValueError(f"seq {i}: {len(t)} blocks hold fewer than kv_len={int(kv[i])} tokens")
+            ids.extend(t[h:w])
+        idv = np.asarray(ids, dtype=np.int64)
+        if int(idv.min()) < 0 or int(idv.max()) >= self.num_blocks:
+            raise IndexError(f"block ids outside [0, {self.num_blocks})")
+        cnt = need[short] - have[short]
+        r = rows[short]
+        first = np.cumsum(cnt) - cnt
+        page = np.arange(idv.shape[0], dtype=np.int64) - np.repeat(first, cnt) + np.repeat(have[short], cnt)
+        self._upd.append((np.repeat(r, cnt).astype(np.int32), page.astype(np.int32), idv.astype(np.int32)))
+        self._n_upd += int(idv.shape[0])
+        rl = r.tolist()
+        if len(set(rl)) < len(rl) or not self._upd_rows.isdisjoint(rl):
+            self._upd_dup = True
+        self._upd_rows.update(rl)
+        self.pages[r] = need[short]
+        return int(idv.shape[0])
 
     # -- assembly -----------------------------------------------------------------
 
@@ -220,11 +243,10 @@ class DeviceBlockTables:
             o = 3 * n
             for part in range(3):
                 h[o + part * nu:o + (part + 1) * nu] = np.concatenate([u[part] for u in self._upd])
-        stream = torch.cuda.current_stream(self.device)
-        N.check(self._lib.pkv_build_batch_meta(self._desc_ref, slot.host.data_ptr(), slot.dev.data_ptr(), n, nu,
-                                               slot.desc_ref, self._status_ptr, stream.cuda_stream),
+        N.check(self._lib.pkv_build_batch_meta(self._desc_ref, slot.host_ptr, slot.dev.data_ptr(), n, nu,
+                                               slot.desc_ref, self._status_ptr, N.raw_stream(self._dev_index)),
                 "build_batch_meta")
-        slot.event.record(stream)
+        slot.event.record(torch.cuda.current_stream(self.device))  # the stream the kernels went to
         slot.used = True
         self._upd.clear()
         self._n_upd = 0

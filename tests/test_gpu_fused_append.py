@@ -121,3 +121,24 @@ def test_slot_that_is_not_the_last_position_is_reported():
     torch.cuda.synchronize()
     with pytest.raises(Exception, match="inconsistent|META_BAD|page table"):
         bks[1].check_status()
+
+
+def test_out_buffer_is_written_in_place_and_checked():
+    """``attend`` / ``append_attend`` with ``out=`` (an optional extension of
+    the reference signature) write the same bits into the caller's buffer and
+    return it; a buffer of the wrong shape, dtype or one overlapping q is refused."""
+    ctx = [40, 300, 17, 600, 1]
+    bks, seqs, m, kn, vn, q = setup(15, ctx, 512)
+    out_a, out_b = run_both(bks, m, kn, vn, q)
+    buf = torch.full((2, *q.shape), float("nan"), dtype=q.dtype, device=q.device)
+    got = bks[0].attend(q, 1, 0.125, m, out=buf[1])
+    torch.cuda.synchronize()
+    assert got.data_ptr() == buf[1].data_ptr()
+    assert torch.equal(buf[1], out_a)
+    assert torch.isnan(buf[0]).all()
+    with pytest.raises(ValueError, match="out must be a contiguous"):
+        bks[0].attend(q, 1, 0.125, m, out=buf[1, :3])
+    with pytest.raises(ValueError, match="out must be a contiguous"):
+        bks[0].attend(q, 1, 0.125, m, out=buf[1].float())
+    with pytest.raises(ValueError, match="must not overlap q"):
+        bks[0].attend(q, 1, 0.125, m, out=q)
