@@ -21,7 +21,7 @@ import pytest
 import torch
 
 from llm_serving_layer_b200 import B200PagedBackend, DeviceBlockTables, build_meta
-from oracle import build_csr, slot_for  # the checker
+from oracle import attend_exact, build_csr, slot_for  # the checker
 
 pytestmark = pytest.mark.gpu
 
@@ -283,3 +283,54 @@ def test_attention_over_device_meta_equals_host_meta(qlens, validate, monkeypatc
     bk.check_status()
     assert bk.last_kernel == ("decode" if max(qlens) == 1 else "prefill")
     assert torch.equal(got, want)
+
+
+@pytest.mark.parametrize("fused", [False, True])
+def test_pipelined_decode_steps_match_oracle(fused):
+    """The serving loop's fast path, checked step by step against the oracle:
+    BatchMeta from DeviceBlockTables (new blocks recorded as sequences cross
+    into a new page), the next step planned (``plan``) right after this step's
+    layers are issued, outputs written into one buffer through ``out=``, four
+    decode steps of 3 layers over a skewed batch."""
+    rs = np.random.RandomState(21 + fused)
+    P, NB, L, Hkv, Hq, D = 16, 3000, 3, 8, 32, 64
+    n = 40
+    ctx = np.clip(np.round(rs.lognormal(np.log(120), 0.9, size=n)), 1, 900).astype(int)
+    steps = 4
+    pages = (ctx + steps + P - 1) // P
+    ids = rs.permutation(NB)[: int(pages.sum())]
+    tables = [t.tolist() for t in np.split(ids, np.cumsum(pages)[:-1])]
+    bk = B200PagedBackend(L, NB, P, Hkv, Hq, D, device=DEV, dtype=torch.float16, validate="device")
+    g = torch.Generator(device=DEV).manual_seed(5)
+    bk._pool.copy_((torch.randn(bk._pool.shape, generator=g, device=DEV) * 0.7).half())
+    bt = DeviceBlockTables(n, int(pages.max()), P, NB, device=DEV, status=bk._status)
+    rows = np.arange(n)
+    for r in range(n):
+        bt.bind(r, tables[r][: (int(ctx[r]) - 1 + P - 1) // P])  # history before the first new token
+    out = torch.empty((L, n, Hq, D), dtype=torch.float16, device=DEV)
+    kv = ctx.copy()
+    bt.extend_to(rows, kv, tables)
+    m = bt.build_batch_meta(rows, np.ones(n), kv)
+    for step in range(steps):
+        q = torch.randn(L, n, Hq, D, generator=g, device=DEV).half()
+        k = (torch.randn(L, n, Hkv, D, generator=g, device=DEV) * 0.7).half()
+        v = (torch.randn(L, n, Hkv, D, generator=g, device=DEV) * 0.7).half()
+        for layer in range(L):
+            if fused:
+                bk.append_attend(layer, k[layer], v[layer], q[layer], 0.125, m, out=out[layer])
+            else:
+                bk.append_kv(layer, k[layer], v[layer], m)
+                bk.attend(q[layer], layer, 0.125, m, out=out[layer])
+        host = build_meta(tables, kv, [1] * n, P)  # the checker's view of this step
+        nkv = kv + 1
+        bt.extend_to(rows, nkv, tables)
+        nm = bt.build_batch_meta(rows, np.ones(n), nkv)
+        bk.plan(nm)  # planned while this step's kernels may still run
+        torch.cuda.synchronize()
+        bk.check_status()
+        for layer in range(L):
+            want = attend_exact(q[layer].cpu().numpy(), bk.k_pool[layer].cpu().numpy(),
+                                bk.v_pool[layer].cpu().numpy(), 0.125, host)
+            err = float(np.abs(out[layer].float().cpu().numpy() - want).max())
+            assert err <= 2e-3, f"step {step} layer {layer}: {err}"
+        kv, m = nkv, nm
