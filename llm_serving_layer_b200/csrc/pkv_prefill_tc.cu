@@ -200,6 +200,19 @@ __global__ void __launch_bounds__(TC_THREADS, 2) prefill_tc_kernel(const __grid_
   const int npages = bad ? 0 : int(npages64);
   const int n_pg = bad ? 0 : tc_tile_pages(kv, ql, j0, TPT);  // pages with keys visible to the tile
   const int nblk = (n_pg + TC_PPB - 1) / TC_PPB;
+  // The softmax threads' query rows, loaded now so the loads travel while the
+  // page ids are checked and the barriers and tensor memory are set up; they
+  // are stored to shared memory (swizzled) further down.
+  const int r_sm = (warp & 3) * 32 + lane;  // a softmax thread's row
+  const int jq_sm = j0 + r_sm % TPT;
+  uint4 qv[8];
+  if (warp >= 2) {
+    const bool qok = !bad && jq_sm < ql;
+    const uint4* src = reinterpret_cast<const uint4*>(static_cast<const T*>(a.q) +
+                                                       ((int64_t(q0) + (qok ? jq_sm : 0)) * a.n_heads + h * G + r_sm / TPT) * TC_D);
+#pragma unroll
+    for (int c = 0; c < 8; ++c) qv[c] = qok ? __ldg(src + c) : make_uint4(0u, 0u, 0u, 0u);
+  }
   if (threadIdx.x == 0) s_bad = bad ? 1 : 0;
   __syncthreads();
   for (int i = threadIdx.x; i < n_pg; i += blockDim.x) {
@@ -342,21 +355,14 @@ __global__ void __launch_bounds__(TC_THREADS, 2) prefill_tc_kernel(const __grid_
   } else {
     // ------------------------------------------------------------ softmax warps
     const int q4 = warp & 3;  // TMEM lane quarter this warp may access
-    const int r = q4 * 32 + lane;
-    const int jq = j0 + r % TPT;
+    const int r = r_sm;
+    const int jq = jq_sm;
     const bool valid = jq < ql;
     const int lim = valid ? kv - ql + jq : -1;  // last visible key of this row
-    {
-      const T* qg = static_cast<const T*>(a.q);
-      const uint4* src = reinterpret_cast<const uint4*>(qg + ((int64_t(q0) + jq) * a.n_heads + h * G + r / TPT) * TC_D);
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        const uint4 v = valid ? __ldg(src + c) : make_uint4(0u, 0u, 0u, 0u);
-        *reinterpret_cast<uint4*>(qs + r * 128 + ((c ^ (r & 7)) << 4)) = v;
-      }
-      fence_proxy_async_smem();
-      mbar_arrive(q_ready);
-    }
+    for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(qs + r * 128 + ((c ^ (r & 7)) << 4)) = qv[c];
+    fence_proxy_async_smem();
+    mbar_arrive(q_ready);
     const uint32_t lane_off = uint32_t(q4 * 32) << 16;
     const float sl2 = a.scale_log2;
     float m = -INFINITY, l = 0.f;
