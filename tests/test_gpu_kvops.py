@@ -256,3 +256,48 @@ def test_swap_many_sequences_llama_geometry_chunked():
         assert torch.equal(got, w)
         assert torch.equal(h.k, w)
         sw.release(h)
+
+
+def test_swap_staging_ring_reuse_with_mixed_sizes():
+    """Staging holding about three victims: several transfers share the ring
+    at once, later chunks wrap to its start and wait only for the uses they
+    overlap. Victims of mixed lengths, asynchronous handles, swap-outs and
+    swap-ins interleaved; everything restored bit-exact into fresh blocks."""
+    L, NB = 16, 1024
+    bk = B200PagedBackend(L, NB, 16, 8, 32, 64, device="cuda:0", dtype=torch.float16)
+    torch.manual_seed(3)
+    bk._pool.copy_(torch.randn(bk._pool.shape, device="cuda:0").half())
+    rs = np.random.RandomState(9)
+    alloc = FifoAllocator(NB, 16, order=rs.permutation(NB))
+    per_block = bk.block_bytes()
+    sw = B200SwapSpace(bk, staging_bytes=3 * 7 * per_block, synchronous=False)
+    seqs = []
+    for i in range(14):
+        s = Seq(alloc, i)
+        s.append(int(rs.randint(20, 200)))
+        seqs.append(s)
+    want = [torch.stack([bk._pool[:, 0, b] for b in s.block_ids], 1).cpu() for s in seqs]
+    handles, dsts = [], []
+    for i, s in enumerate(seqs):
+        handles.append(sw.swap_out(f"r{i}", s))
+        s.free()
+        if i % 3 == 2:  # a restore of an earlier victim between the swap-outs
+            j = len(dsts)
+            d = Seq(alloc, 100 + j)
+            d.append(handles[j].num_tokens)
+            sw.swap_in(handles[j], d)
+            dsts.append(d)
+    while len(dsts) < len(handles):
+        j = len(dsts)
+        d = Seq(alloc, 100 + j)
+        d.append(handles[j].num_tokens)
+        sw.swap_in(handles[j], d)
+        dsts.append(d)
+    sw.wait()
+    torch.cuda.synchronize()
+    bk.check_status()
+    for w, d, h in zip(want, dsts, handles):
+        got = torch.stack([bk._pool[:, 0, b] for b in d.block_ids], 1).cpu()
+        assert torch.equal(got, w)
+        assert torch.equal(h.k, w)
+        sw.release(h)
