@@ -149,6 +149,34 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
 #undef PKV_R8
 #undef PKV_W8
 
+// Packed fp32 pairs (sm_100's two-wide FMA / add) and a three-input max: the
+// softmax threads are bound by instruction issue, so each pair of scores
+// takes one FMA and one add instead of two each.
+__device__ __forceinline__ unsigned long long f32x2(float a, float b) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void f32x2_split(unsigned long long v, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ unsigned long long fma_f32x2(unsigned long long a, unsigned long long b,
+                                                        unsigned long long c) {
+  unsigned long long d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ unsigned long long add_f32x2(unsigned long long a, unsigned long long b) {
+  unsigned long long d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 __device__ __forceinline__ int tc_tile_pages(int64_t kv, int ql, int j0, int qt) {
   if (kv < ql || ql < 1) return 0;
   const int jl = min(j0 + qt, ql) - 1;
@@ -396,8 +424,9 @@ __global__ void __launch_bounds__(TC_THREADS, 2) prefill_tc_kernel(const __grid_
 #pragma unroll
         for (int u = 0; u < 8; ++u) t[u] = __uint_as_float(sr[u]);
 #pragma unroll
-        for (int i = 8; i < 64; ++i) t[i & 7] = fmaxf(t[i & 7], __uint_as_float(sr[i]));
-        mx = fmaxf(fmaxf(fmaxf(t[0], t[1]), fmaxf(t[2], t[3])), fmaxf(fmaxf(t[4], t[5]), fmaxf(t[6], t[7])));
+        for (int i = 8; i < 64; i += 2)
+          t[(i >> 1) & 7] = max3f(t[(i >> 1) & 7], __uint_as_float(sr[i]), __uint_as_float(sr[i + 1]));
+        mx = max3f(max3f(t[0], t[1], t[2]), max3f(t[3], t[4], t[5]), fmaxf(t[6], t[7]));
       }
       const float sc = sl2 > 0.f ? sl2 : 1.f;  // the scale still to apply (log2 units)
       mx = mx * sc;                            // -inf stays -inf (sc > 0)
@@ -424,17 +453,20 @@ __global__ void __launch_bounds__(TC_THREADS, 2) prefill_tc_kernel(const __grid_
         }
       }
       const float mu = m == -INFINITY ? 0.f : m;
-      float lt[8];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) lt[u] = 0.f;
+      const unsigned long long sc2 = f32x2(sc, sc), nmu2 = f32x2(-mu, -mu);
+      unsigned long long lt2[4] = {0ull, 0ull, 0ull, 0ull};  // pairs of running sums (0.f bits)
       uint32_t pk[32];
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
-        const float p0 = ex2(fmaf(__uint_as_float(sr[2 * i]), sc, -mu));
-        const float p1 = ex2(fmaf(__uint_as_float(sr[2 * i + 1]), sc, -mu));
-        lt[i & 7] += p0 + p1;
+        float x0, x1;
+        f32x2_split(fma_f32x2(f32x2(__uint_as_float(sr[2 * i]), __uint_as_float(sr[2 * i + 1])), sc2, nmu2), x0, x1);
+        const float p0 = ex2(x0), p1 = ex2(x1);
+        lt2[i & 3] = add_f32x2(lt2[i & 3], f32x2(p0, p1));
         pk[i] = MmaOp<T>::pack(p0, p1);
       }
+      float lt[8];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) f32x2_split(lt2[u], lt[2 * u], lt[2 * u + 1]);
       const float ls = ((lt[0] + lt[1]) + (lt[2] + lt[3])) + ((lt[4] + lt[5]) + (lt[6] + lt[7]));
       l += ls;
       tmem_st32(tbase + lane_off + b * TC_KB, pk);
