@@ -632,7 +632,6 @@ def run_e2e(torch, bk, tables, ctx, args, device, ws, dist, n_graphs, meta_mode=
         m = nxt.pop(s) if s in nxt else meta_for_step(s)
         if s not in staged:
             h2d(s)
-        h2d(s + 1)  # the next step's inputs travel while this step computes
         staged.discard(s)
         b = s % 2
         comp.wait_event(ev_ready[b])
@@ -642,6 +641,10 @@ def run_e2e(torch, bk, tables, ctx, args, device, ws, dist, n_graphs, meta_mode=
             else:
                 bk.append_kv(layer, dk[b][layer], dv[b][layer], m)
                 bk.attend(dq[b][layer], layer, SCALE, m, out=dout[layer])
+            if layer == 0:
+                # the next step's inputs travel while this step computes; issued
+                # after the first layer's launches so that those are not delayed
+                h2d(s + 1)
             if layer % GROUP == GROUP - 1:
                 ev_out[layer].record(comp)
         ev_free[b].record(comp)
