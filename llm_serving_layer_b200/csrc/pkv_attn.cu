@@ -119,15 +119,20 @@ __global__ void plan_kernel(const int32_t* __restrict__ kv_indptr,
   }
   if (bad) {
     if (lane == 0) flag(st, PKV_DEV_META_BAD);
-    return;
+  } else {
+    for (int64_t p = a + lane; p < b; p += 32) {
+      const int id = kv_indices[p];
+      if (id < 0 || id >= num_blocks) flag(st, PKV_DEV_SLOT_OOB);
+      const int first = (p == a), last = (p == b - 1);
+      const int valid = last ? lpl : block_size;
+      desc[p] = make_int4(id, (s << 7) | (first << 6) | (last << 5) | valid, int(a), int(b));
+    }
   }
-  for (int64_t p = a + lane; p < b; p += 32) {
-    const int id = kv_indices[p];
-    if (id < 0 || id >= num_blocks) flag(st, PKV_DEV_SLOT_OOB);
-    const int first = (p == a), last = (p == b - 1);
-    const int valid = last ? lpl : block_size;
-    desc[p] = make_int4(id, (s << 7) | (first << 6) | (last << 5) | valid, int(a), int(b));
-  }
+  // The decode kernel reads the descriptors before its griddepcontrol.wait (it
+  // starts only once this kernel has completed, which never triggers its
+  // dependents early): the stores are made visible at GPU scope before the
+  // block exits.
+  __threadfence();
 }
 
 // ---------------------------------------------------------------- decode
@@ -404,7 +409,9 @@ __global__ void __maxnreg__(DK_MAXNREG) decode_kernel(const __grid_constant__ CU
   // the device, so their count is read there (bounded by the descriptor capacity).
   // The ranges are cut over G = min(grid, P) CTAs, so every range is non-empty
   // (a split sequence's pieces are exactly the CTAs cf..cl); surplus CTAs exit.
-  const int64_t P = a.p_dev ? max(int64_t(0), min(*a.p_dev, a.total_pages)) : a.total_pages;
+  // (L2-level loads, ld.global.cg: nothing here may come from a line this SM
+  // cached in L1 before the plan rewrote it)
+  const int64_t P = a.p_dev ? max(int64_t(0), min(__ldcg(a.p_dev), a.total_pages)) : a.total_pages;
   const int G = int(min(int64_t(gridDim.x), P));
   const int c = blockIdx.x;
   if (c >= G) return;
@@ -416,7 +423,7 @@ __global__ void __maxnreg__(DK_MAXNREG) decode_kernel(const __grid_constant__ CU
   // sequence (head piece H) may be cut by the range's ends; T is taken first,
   // then H, then the middle M, so that cut pieces are handed to the merge warp
   // early and their merges overlap the consumers' remaining pages.
-  const int4 dfirst = a.desc[p0], dlast = a.desc[p1 - 1];
+  const int4 dfirst = __ldcg(a.desc + p0), dlast = __ldcg(a.desc + p1 - 1);
   const int sf = dfirst.y >> 7, sl = dlast.y >> 7;
   int lenT = 0, lenH = 0;
   int64_t hend = p0, tstart = p1;
@@ -438,7 +445,7 @@ __global__ void __maxnreg__(DK_MAXNREG) decode_kernel(const __grid_constant__ CU
   };
   const int kv_coord = 2 * a.layer;
   if (warp == n_cons && lane < min(R, a.prefetch)) {
-    const int id = a.desc[pos(lane)].x;
+    const int id = __ldcg(&a.desc[pos(lane)].x);
     if (id >= 0) {
       tma_prefetch_l2_4d(&tmap, 0, id * DK_P, 0, kv_coord);
       tma_prefetch_l2_4d(&tmap, 0, id * DK_P, 0, kv_coord + 1);

@@ -120,6 +120,7 @@ __global__ void __launch_bounds__(1024) prefill_plan_kernel(
       *n_tiles = 0;
       if (mixed) *mo.p_dec = 0;
     }
+    __threadfence();  // p_dec is read by the decode kernel before its griddepcontrol.wait
     return;
   }
   // exclusive scan over the buckets from the most expensive down: thread t owns
@@ -196,6 +197,11 @@ __global__ void __launch_bounds__(1024) prefill_plan_kernel(
   }
   for (int d = base_seq + tid; d < n_seqs; d += blockDim.x) mo.rows[d] = -1;
   if (tid == 0) *mo.p_dec = base_pg;
+  // The decode kernel reads p_dec and the descriptors before its
+  // griddepcontrol.wait (it starts only once this kernel has completed, which
+  // never triggers its dependents early): the stores are made visible at GPU
+  // scope before this block exits.
+  __threadfence();
 }
 
 // ---------------------------------------------------------------- attention
