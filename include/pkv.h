@@ -157,6 +157,42 @@ PKV_API int pkv_append_attend_planned(const pkv_pool* pool, int32_t layer, int32
                               float scale, const pkv_batch* batch, int32_t decode_hint, void* workspace,
                               size_t workspace_bytes, void* stream);
 
+/* Rotary position embedding of q and k at each token's position, the step the
+ * engine runs on the projected q and k before append_kv / attend
+ * (docs/ARCHITECTURE.md:167-172: project Q/K/V, RoPE at meta.positions,
+ * append, attend; the engine itself is not in the reference tree). q [n_tokens]
+ * [n_heads][head_dim] and k [n_tokens][n_kv_heads][head_dim] (dtype PKV_F16 or
+ * PKV_BF16, contiguous) are rotated into q_out / k_out (which may equal q / k:
+ * in place); either tensor may be skipped with 0 heads. Pair (i, i + D/2) of
+ * each head of token t is rotated by the angle whose cosine / sine are
+ * rope_cos / rope_sin[positions[t]][i] (fp32 tables [rope_max_pos][D/2]):
+ * a' = a*cos - b*sin, b' = a*sin + b*cos, every product rounded to fp32 before
+ * the difference / sum, then rounded to the dtype (nearest even) — the same
+ * bits as that formula evaluated elementwise in fp32. One launch on `stream`.
+ * A position outside [0, rope_max_pos) leaves its token unrotated and sets
+ * PKV_DEV_META_BAD in *dev_status. */
+PKV_API int pkv_rope(int32_t dtype, const void* q, void* q_out, int32_t n_heads, const void* k, void* k_out,
+                     int32_t n_kv_heads, int64_t n_tokens, int32_t head_dim, const int64_t* positions,
+                     const float* rope_cos, const float* rope_sin, int64_t rope_max_pos, int32_t* dev_status,
+                     void* stream);
+
+/* pkv_append_attend_planned with the rotary embedding fused in: q and k are
+ * given BEFORE rotation, and the single decode launch rotates each row's q as
+ * it loads it and each new K row as it writes it to its slot (tables and
+ * rounding as pkv_rope; head_dim 64, so the tables are [rope_max_pos][32],
+ * 16-byte aligned). The pool receives the rotated K; q and k are not changed.
+ * Same results, bit for bit, as pkv_rope followed by pkv_append_attend_planned.
+ * Batches the fused launch does not take (anything but a decode batch on the
+ * decode kernel's geometry with 16-byte aligned k and v) return
+ * PKV_ERR_UNSUPPORTED with nothing launched: the caller runs those two calls.
+ * Replaces the engine's separate RoPE op and append_kv call per layer
+ * (docs/ARCHITECTURE.md:167-172); no counterpart in the reference itself. */
+PKV_API int pkv_append_attend_rope_planned(const pkv_pool* pool, int32_t layer, int32_t n_heads, const void* k,
+                                   const void* v, const int32_t* slot_mapping, const void* q, void* out,
+                                   float scale, const pkv_batch* batch, int32_t decode_hint, void* workspace,
+                                   size_t workspace_bytes, const int64_t* positions, const float* rope_cos,
+                                   const float* rope_sin, int64_t rope_max_pos, void* stream);
+
 /* Which kernel pkv_attend_planned runs for a batch of this shape and hint
  * (host only, nothing touches the device): PKV_KERNEL_GENERIC,
  * PKV_KERNEL_DECODE or PKV_KERNEL_PREFILL; -PKV_ERR_ARG for a bad pool. No

@@ -104,6 +104,8 @@ class B200PagedBackend:
         self._dev_index = self.device.index if self.device.index is not None else torch.cuda.current_device()
         self._slots_meta: Any = None  # the meta whose int32 slot map is cached in _slots
         self._slots: torch.Tensor | None = None
+        self._pos_meta: Any = None  # the meta whose int64 device positions are cached in _pos
+        self._pos: torch.Tensor | None = None
         self._ws: torch.Tensor | None = None
         # per-step state, keyed by BatchMeta identity (a strong reference keeps
         # the id from being recycled while it is cached)
@@ -188,12 +190,22 @@ class B200PagedBackend:
                                         N.raw_stream(self._dev_index)), "append_kv")
 
     def append_attend(self, layer_idx: int, k: torch.Tensor, v: torch.Tensor, q: torch.Tensor,
-                      scale: float, meta: Any, *, out: torch.Tensor | None = None) -> torch.Tensor:
+                      scale: float, meta: Any, *, out: torch.Tensor | None = None,
+                      rope: tuple[torch.Tensor, torch.Tensor] | None = None) -> torch.Tensor:
         """``append_kv(layer_idx, k, v, meta)`` then ``attend(q, layer_idx, scale,
         meta)`` in one call, with the same checks, errors and results. A decode
         step is ONE kernel launch: the decode kernel writes each sequence's new
         K/V row to its slot and attends over it (no reference counterpart; the
-        engine makes the two calls, ``docs/ARCHITECTURE.md:167-172``)."""
+        engine makes the two calls, ``docs/ARCHITECTURE.md:167-172``).
+
+        ``rope=(cos, sin)``: q and k are given before the rotary embedding, which
+        is applied at ``meta.positions`` with these fp32 tables
+        ``[max_pos, head_dim // 2]`` (see ``rope``); the pool receives the
+        rotated K and the result is that of ``rope`` followed by this call, bit
+        for bit. For a decode step the rotation happens inside the single
+        launch; other steps run ``rope`` first (one launch for q and k)."""
+        if rope is not None:
+            return self._append_attend_rope(layer_idx, k, v, q, scale, meta, out, rope)
         k, v, slots, tokens = self._append_args(layer_idx, k, v, meta)
         if q.shape != (tokens, self.n_heads, self.head_dim):
             raise ValueError(
@@ -213,6 +225,90 @@ class B200PagedBackend:
             out.data_ptr(), float(scale), st["batch_ref"], st["hint"], st["ws_ptr"], st["ws_bytes"],
             N.raw_stream(self._dev_index)), "append_attend")
         return out
+
+    def _append_attend_rope(self, layer_idx, k, v, q, scale, meta, out, rope) -> torch.Tensor:
+        cos, sin, pos = self._rope_args(rope, meta)
+        k, v, slots, tokens = self._append_args(layer_idx, k, v, meta)
+        if pos.shape[0] != tokens:
+            raise ValueError(f"meta.positions has {pos.shape[0]} entries but {tokens} tokens were supplied")
+        if q.shape != (tokens, self.n_heads, self.head_dim):
+            raise ValueError(
+                f"q has shape {tuple(q.shape)}, expected ({tokens}, {self.n_heads}, {self.head_dim})"
+            )
+        st = self._step_state(meta)
+        if st["n_tokens"] != tokens:
+            raise ValueError(f"meta describes {st['n_tokens']} tokens but q has {tokens}")
+        q = self._own(q, self.dtype)
+        out = self._out(q, out)
+        if tokens == 0:
+            return out
+        rc = self._lib.pkv_append_attend_rope_planned(
+            self._pdesc, layer_idx, self.n_heads, k.data_ptr(), v.data_ptr(), slots.data_ptr(), q.data_ptr(),
+            out.data_ptr(), float(scale), st["batch_ref"], st["hint"], st["ws_ptr"], st["ws_bytes"],
+            pos.data_ptr(), cos.data_ptr(), sin.data_ptr(), cos.shape[0], N.raw_stream(self._dev_index))
+        if rc == N.PKV_ERR_UNSUPPORTED:  # not a single-launch decode step: rotate, then the plain call
+            q, k = self.rope(q, k, meta, rope)
+            return self.append_attend(layer_idx, k, v, q, scale, meta, out=out)
+        N.check(rc, "append_attend")
+        self.n_runs += 1
+        self.last_kernel = st["kernel"]
+        return out
+
+    def rope(self, q: torch.Tensor | None, k: torch.Tensor | None, meta: Any,
+             rope: tuple[torch.Tensor, torch.Tensor]) -> tuple[torch.Tensor | None, torch.Tensor | None]:
+        """Rotary position embedding of q ``(T, n_heads, head_dim)`` and k
+        ``(T, n_kv_heads, head_dim)`` at ``meta.positions``, returned as new
+        tensors in the pool dtype (either input may be None). ``rope = (cos,
+        sin)``: fp32 tables ``[max_pos, head_dim // 2]`` on this device; pair
+        (i, i + head_dim/2) of each head of token t is rotated by
+        cos/sin[positions[t], i] — ``a*cos - b*sin, a*sin + b*cos`` with each
+        product rounded to fp32, then rounded to the pool dtype, the bits of
+        that formula evaluated elementwise in fp32. One kernel launch
+        (``pkv_rope``). A position outside the tables raises on the next
+        ``check_status`` (and leaves its token unrotated)."""
+        cos, sin, pos = self._rope_args(rope, meta)
+        T = int(pos.shape[0])
+        qo = ko = None
+        args = []
+        for x, heads, name in ((q, self.n_heads, "q"), (k, self.n_kv_heads, "k")):
+            if x is None:
+                args.append((None, None, 0))
+                continue
+            if x.shape != (T, heads, self.head_dim):
+                raise ValueError(f"{name} has shape {tuple(x.shape)}, expected ({T}, {heads}, {self.head_dim})")
+            x = self._own(x, self.dtype)
+            y = torch.empty_like(x)
+            args.append((x, y, heads))
+        (xq, qo, hq), (xk, ko, hk) = args
+        N.check(self._lib.pkv_rope(
+            N.DTYPE_CODE[self.dtype], N.ptr(xq), N.ptr(qo), hq, N.ptr(xk), N.ptr(ko), hk, T, self.head_dim,
+            pos.data_ptr(), cos.data_ptr(), sin.data_ptr(), cos.shape[0], self._status_ptr,
+            N.raw_stream(self._dev_index)), "rope")
+        return qo, ko
+
+    def _rope_args(self, rope, meta):
+        try:
+            cos, sin = rope
+        except (TypeError, ValueError):
+            raise ValueError("rope must be a (cos, sin) pair of tensors") from None
+        half = self.head_dim // 2
+        for t, name in ((cos, "cos"), (sin, "sin")):
+            if (not isinstance(t, torch.Tensor) or t.dim() != 2 or t.shape[1] != half or t.shape[0] < 1
+                    or t.dtype != torch.float32 or not t.is_cuda or t.get_device() != self._dev_index
+                    or not t.is_contiguous() or t.data_ptr() % 16):
+                raise ValueError(
+                    f"rope {name} must be a contiguous 16-byte aligned float32 [max_pos, {half}] tensor on "
+                    f"{self.device}")
+        if cos.shape != sin.shape:
+            raise ValueError(f"rope cos {tuple(cos.shape)} and sin {tuple(sin.shape)} differ in shape")
+        if getattr(meta, "positions", None) is None:
+            raise ValueError("the rotary embedding needs meta.positions")
+        if self._pos_meta is not meta:  # the int64 device positions, once per meta
+            self._pos = self._own(meta.positions, torch.int64)
+            if self._pos.dim() != 1:
+                raise ValueError("meta.positions must be one-dimensional")
+            self._pos_meta = meta
+        return cos, sin, self._pos
 
     def _append_args(self, layer_idx: int, k: torch.Tensor, v: torch.Tensor, meta: Any):
         self._check_layer(layer_idx)
@@ -399,6 +495,8 @@ class B200PagedBackend:
         self._meta_state = {}
         self._slots_meta = None
         self._slots = None
+        self._pos_meta = None
+        self._pos = None
 
     # -- status -----------------------------------------------------------------
 

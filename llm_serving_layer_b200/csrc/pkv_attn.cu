@@ -155,6 +155,14 @@ struct DecodeArgs {
   char* k_slab;          // this layer's K / V slab (slot * row_bytes addresses a row)
   char* v_slab;
   int64_t n_slots;
+  // Fused rotary embedding (rcos NULL: none; only with the fused KV-append): the
+  // q row and the new K row of token `row` are rotated at position positions[row]
+  // by the angles whose cosines / sines are rcos / rsin[pos][0 .. 31] (pairs
+  // (i, i + 32) of each head), positions outside [0, rmax) flagged.
+  const int64_t* positions = nullptr;
+  const float* rcos = nullptr;
+  const float* rsin = nullptr;
+  int64_t rmax = 0;
   int64_t total_pages;   // capacity of desc (and the page count when p_dev is NULL)
   int n_seqs;
   int n_rows;            // rows of q / out
@@ -187,6 +195,27 @@ __device__ __forceinline__ void load_q_frag(const T* __restrict__ q, int row, in
 #pragma unroll
     for (int ks = 0; ks < 4; ++ks) qb[ks][0] = qb[ks][1] = 0u;
   }
+}
+
+// Rotary embedding of a q fragment (see load_q_frag): the lane holds dims
+// 2*c4 + 16*ks + {0, 1} in qb[ks][0] and 2*c4 + 16*ks + 8 + {0, 1} in
+// qb[ks][1]; dim i < 32 pairs with dim i + 32, which the same lane holds in
+// qb[ks + 2]. cs / sn: the token's 32 cosines / sines.
+template <typename T>
+__device__ __forceinline__ void rope_q_frag(uint32_t (&qb)[4][2], int c4, const float* cs, const float* sn) {
+#pragma unroll
+  for (int ks = 0; ks < 2; ++ks)
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+      const int i = 2 * c4 + 16 * ks + 8 * hf;
+      const float2 c = __ldg(reinterpret_cast<const float2*>(cs + i));
+      const float2 sv = __ldg(reinterpret_cast<const float2*>(sn + i));
+      float2 lo = unpack2<T>(qb[ks][hf]), hi = unpack2<T>(qb[ks + 2][hf]);
+      rope_pair(lo.x, hi.x, c.x, sv.x);
+      rope_pair(lo.y, hi.y, c.y, sv.y);
+      qb[ks][hf] = pack2<T>(lo.x, lo.y);
+      qb[ks + 2][hf] = pack2<T>(hi.x, hi.y);
+    }
 }
 
 // Consumer warp h merges the split-K pieces in CTAs cf..cl of a sequence
@@ -551,9 +580,48 @@ __global__ void __maxnreg__(DK_MAXNREG) decode_kernel(const __grid_constant__ CU
               const uint4* vs = reinterpret_cast<const uint4*>(static_cast<const char*>(a.vnew) + row * rb);
               uint4* kd = reinterpret_cast<uint4*>(a.k_slab + slot * rb);
               uint4* vd = reinterpret_cast<uint4*>(a.v_slab + slot * rb);
-              for (int e = lane; e < int(rb / 16); e += 32) {
-                kd[e] = __ldg(ks + e);
-                vd[e] = __ldg(vs + e);
+              const float* cs = nullptr;
+              const float* sn = nullptr;
+              if (a.rcos) {
+                const int64_t tp = __ldg(a.positions + row);
+                if (tp >= 0 && tp < a.rmax) {
+                  cs = a.rcos + tp * (DK_D / 2);
+                  sn = a.rsin + tp * (DK_D / 2);
+                } else if (lane == 0) {
+                  flag(a.st, PKV_DEV_META_BAD);  // the row is stored unrotated
+                }
+              }
+              if (cs) {
+                // lane = (head, chunk j): dims 8j .. 8j + 7 (uint4 j of the head's
+                // row) pair with dims 32 + 8j .. (uint4 j + 4)
+                const int hh = lane >> 2, j = lane & 3;
+                if (hh < n_cons) {
+                  const uint4 lo = __ldg(ks + hh * 8 + j), hi = __ldg(ks + hh * 8 + j + 4);
+                  const float4 c0 = __ldg(reinterpret_cast<const float4*>(cs + 8 * j));
+                  const float4 c1 = __ldg(reinterpret_cast<const float4*>(cs + 8 * j + 4));
+                  const float4 s0 = __ldg(reinterpret_cast<const float4*>(sn + 8 * j));
+                  const float4 s1 = __ldg(reinterpret_cast<const float4*>(sn + 8 * j + 4));
+                  const uint32_t lw[4] = {lo.x, lo.y, lo.z, lo.w}, hw[4] = {hi.x, hi.y, hi.z, hi.w};
+                  const float cc[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+                  const float ss[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+                  uint32_t ol[4], oh[4];
+#pragma unroll
+                  for (int w2 = 0; w2 < 4; ++w2) {
+                    float2 x = unpack2<T>(lw[w2]), y = unpack2<T>(hw[w2]);
+                    rope_pair(x.x, y.x, cc[2 * w2], ss[2 * w2]);
+                    rope_pair(x.y, y.y, cc[2 * w2 + 1], ss[2 * w2 + 1]);
+                    ol[w2] = pack2<T>(x.x, x.y);
+                    oh[w2] = pack2<T>(y.x, y.y);
+                  }
+                  kd[hh * 8 + j] = make_uint4(ol[0], ol[1], ol[2], ol[3]);
+                  kd[hh * 8 + j + 4] = make_uint4(oh[0], oh[1], oh[2], oh[3]);
+                }
+                for (int e = lane; e < int(rb / 16); e += 32) vd[e] = __ldg(vs + e);
+              } else {
+                for (int e = lane; e < int(rb / 16); e += 32) {
+                  kd[e] = __ldg(ks + e);
+                  vd[e] = __ldg(vs + e);
+                }
               }
               asm volatile("fence.proxy.async.global;" ::: "memory");
             }
@@ -632,6 +700,16 @@ __global__ void __maxnreg__(DK_MAXNREG) decode_kernel(const __grid_constant__ CU
   uint32_t qb[4][2], qn[4][2];
   int nxt_seq = -1, nxt_row = -1;
   auto row_of = [&](int sq) -> int { return a.rows ? __ldg(a.rows + sq) : sq; };
+  auto load_q = [&](int row, uint32_t (&dst)[4][2]) {
+    load_q_frag<T, GROUPS>(q, row, a.n_heads, h, g, c4, dst);
+    if constexpr (FUSE) {
+      if (a.rcos && g < GROUPS) {
+        const int64_t tp = __ldg(a.positions + row);
+        if (tp >= 0 && tp < a.rmax) rope_q_frag<T>(dst, c4, a.rcos + tp * (DK_D / 2), a.rsin + tp * (DK_D / 2));
+        else flag(a.st, PKV_DEV_META_BAD);
+      }
+    }
+  };
   const int first_seq = dfirst.y >> 7;  // its piece (if split) uses partial slot 0
   const int k_tok = (lane & 7) + ((lane >> 3) & 1) * 8, k_chk = lane >> 4;
   const int v_tok = (lane & 7) + (lane >> 4) * 8, v_chk = (lane >> 3) & 1;
@@ -659,12 +737,12 @@ __global__ void __maxnreg__(DK_MAXNREG) decode_kernel(const __grid_constant__ CU
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks) { qb[ks][0] = qn[ks][0]; qb[ks][1] = qn[ks][1]; }
     } else {
-      load_q_frag<T, GROUPS>(q, row, a.n_heads, h, g, c4, qb);
+      load_q(row, qb);
     }
     // the sequence processed next: H's after T, then each M in turn
     nxt_seq = (i < lenT) ? sf : seq + 1;
     nxt_row = (nxt_seq >= 0 && nxt_seq < a.n_seqs) ? row_of(nxt_seq) : -1;
-    if (nxt_row >= 0 && nxt_row < a.n_rows) load_q_frag<T, GROUPS>(q, nxt_row, a.n_heads, h, g, c4, qn);
+    if (nxt_row >= 0 && nxt_row < a.n_rows) load_q(nxt_row, qn);
     else nxt_seq = -1;
     float o[4][4];
 #pragma unroll
@@ -1289,10 +1367,18 @@ extern "C" int pkv_attend_kernel(const pkv_pool* pool, int32_t n_heads, int32_t 
   return PKV_KERNEL_GENERIC;
 }
 
-extern "C" int pkv_append_attend_planned(const pkv_pool* pool, int32_t layer, int32_t n_heads, const void* k,
-                                         const void* v, const int32_t* slot_mapping, const void* q, void* out,
-                                         float scale, const pkv_batch* batch, int32_t decode_hint, void* workspace,
-                                         size_t workspace_bytes, void* stream) {
+namespace {
+struct RopeIn {  // fused rotary embedding: none when cos is NULL
+  const int64_t* positions;
+  const float* cos;
+  const float* sin;
+  int64_t max_pos;
+};
+
+int append_attend_impl(const pkv_pool* pool, int32_t layer, int32_t n_heads, const void* k, const void* v,
+                       const int32_t* slot_mapping, const void* q, void* out, float scale, const pkv_batch* batch,
+                       int32_t decode_hint, void* workspace, size_t workspace_bytes, const RopeIn& rope,
+                       void* stream) {
   if (int rc = check_pool(pool)) return rc;
   const pkv_pool& p = *pool;
   if (layer < 0 || layer >= p.num_layers)
@@ -1305,6 +1391,11 @@ extern "C" int pkv_append_attend_planned(const pkv_pool* pool, int32_t layer, in
   const bool fused = decode_hint == 1 && decode_supported(p, n_heads) && batch->n_tokens == batch->n_seqs &&
                      batch->total_pages > 0 &&
                      ((reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v)) & 15) == 0;
+  if (!fused && rope.cos)
+    return fail(PKV_ERR_UNSUPPORTED,
+                "the rotary embedding is fused only into a decode batch's single launch (decode_hint 1, the decode "
+                "kernel's geometry, 16-byte aligned k and v); rotate q and k with pkv_rope and call "
+                "pkv_append_attend_planned");
   if (!fused) {  // the two calls the fused launch replaces
     if (int rc = pkv_append_kv(pool, layer, k, v, slot_mapping, batch->n_tokens, batch->dev_status, stream))
       return rc;
@@ -1336,6 +1427,10 @@ extern "C" int pkv_append_attend_planned(const pkv_pool* pool, int32_t layer, in
   a.k_slab = static_cast<char*>(p.base) + (2 * int64_t(layer)) * sb;
   a.v_slab = a.k_slab + sb;
   a.n_slots = p.num_blocks * p.block_size;
+  a.positions = rope.positions;
+  a.rcos = rope.cos;
+  a.rsin = rope.sin;
+  a.rmax = rope.max_pos;
   a.total_pages = batch->total_pages;
   a.n_seqs = batch->n_seqs;
   a.n_rows = batch->n_tokens;
@@ -1346,6 +1441,31 @@ extern "C" int pkv_append_attend_planned(const pkv_pool* pool, int32_t layer, in
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (p.dtype == PKV_F16) return launch_decode_g<__half>(p, groups, tm, a, batch->total_pages, s);
   return launch_decode_g<__nv_bfloat16>(p, groups, tm, a, batch->total_pages, s);
+}
+}  // namespace
+
+extern "C" int pkv_append_attend_planned(const pkv_pool* pool, int32_t layer, int32_t n_heads, const void* k,
+                                         const void* v, const int32_t* slot_mapping, const void* q, void* out,
+                                         float scale, const pkv_batch* batch, int32_t decode_hint, void* workspace,
+                                         size_t workspace_bytes, void* stream) {
+  return append_attend_impl(pool, layer, n_heads, k, v, slot_mapping, q, out, scale, batch, decode_hint, workspace,
+                            workspace_bytes, RopeIn{nullptr, nullptr, nullptr, 0}, stream);
+}
+
+extern "C" int pkv_append_attend_rope_planned(const pkv_pool* pool, int32_t layer, int32_t n_heads, const void* k,
+                                              const void* v, const int32_t* slot_mapping, const void* q, void* out,
+                                              float scale, const pkv_batch* batch, int32_t decode_hint,
+                                              void* workspace, size_t workspace_bytes, const int64_t* positions,
+                                              const float* rope_cos, const float* rope_sin, int64_t rope_max_pos,
+                                              void* stream) {
+  if (!positions || !rope_cos || !rope_sin)
+    return fail(PKV_ERR_ARG, "positions, rope_cos and rope_sin must be non-NULL");
+  if (rope_max_pos <= 0) return fail(PKV_ERR_ARG, "rope_max_pos must be positive");
+  if ((reinterpret_cast<uintptr_t>(rope_cos) | reinterpret_cast<uintptr_t>(rope_sin)) & 15)
+    return fail(PKV_ERR_ARG, "rope_cos and rope_sin must be 16-byte aligned");
+  if (reinterpret_cast<uintptr_t>(positions) & 7) return fail(PKV_ERR_ARG, "positions must be 8-byte aligned");
+  return append_attend_impl(pool, layer, n_heads, k, v, slot_mapping, q, out, scale, batch, decode_hint, workspace,
+                            workspace_bytes, RopeIn{positions, rope_cos, rope_sin, rope_max_pos}, stream);
 }
 
 extern "C" int pkv_attend(const pkv_pool* pool, int32_t layer, int32_t n_heads, const void* q,

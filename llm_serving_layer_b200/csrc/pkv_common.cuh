@@ -307,4 +307,39 @@ __device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float x) { return
 template <>
 __device__ __forceinline__ float from_f<float>(float x) { return x; }
 
+// Rotary embedding of one pair (a, b) = (x[i], x[i + D/2]) by the angle whose
+// cosine is c and sine s: a' = a*c - b*s, b' = a*s + b*c, with every product
+// rounded to fp32 before the difference / sum (no fused multiply-add), which is
+// how the fp32 elementwise evaluation of that formula rounds.
+__device__ __forceinline__ void rope_pair(float& a, float& b, float c, float s) {
+  const float ra = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
+  const float rb = __fadd_rn(__fmul_rn(a, s), __fmul_rn(b, c));
+  a = ra;
+  b = rb;
+}
+
+// two 16-bit values packed in a word (lower index in the low half) <-> floats
+template <typename T>
+__device__ __forceinline__ float2 unpack2(uint32_t u);
+template <>
+__device__ __forceinline__ float2 unpack2<__half>(uint32_t u) {
+  return __half22float2(*reinterpret_cast<const __half2*>(&u));
+}
+template <>
+__device__ __forceinline__ float2 unpack2<__nv_bfloat16>(uint32_t u) {
+  return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u));
+}
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi);
+template <>
+__device__ __forceinline__ uint32_t pack2<__half>(float lo, float hi) {
+  const __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+template <>
+__device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float lo, float hi) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
 }  // namespace pkv

@@ -10,7 +10,9 @@ reference tree and no weights ship with it. This module is a stand-in with the
 same structure and interface (``docs/ARCHITECTURE.md:167-172``: per layer
 project Q/K/V, RoPE at ``meta.positions``, ``backend.append_kv`` then
 ``backend.attend``, output projection, residual; logits gathered at
-``meta.last_token_ix``), at Llama-3.2-1B geometry: hidden 2048, 16 layers,
+``meta.last_token_ix``; with a backend that takes ``rope=``, the RoPE, append
+and attention of a layer are one ``append_attend`` call, one kernel launch for
+a decode step), at Llama-3.2-1B geometry: hidden 2048, 16 layers,
 32 query / 8 KV heads of 64, SwiGLU FFN 8192, vocab 128256, RMSNorm eps 1e-5,
 RoPE theta 500000 (plain rotary frequencies, no long-context rescaling), tied
 input/output embedding, fp16. Weights are drawn from a seeded N(0, init_std²).
@@ -47,6 +49,7 @@ class LlamaConfig:
     vocab: int = 128256
     rope_theta: float = 500000.0
     eps: float = 1e-5
+    rope_positions: int = 16384  # rows of the cosine / sine tables (largest position + 1)
 
 
 class RandomLlama:
@@ -54,7 +57,7 @@ class RandomLlama:
 
     def __init__(self, cfg: LlamaConfig = LlamaConfig(), device: str | torch.device = "cuda:0",
                  dtype: torch.dtype = torch.float16, seed: int = 0, init_std: float = 0.02,
-                 row_norm_sigma: float = 0.0, fp32_head: bool = False):
+                 row_norm_sigma: float = 0.0, fp32_head: bool = False, fused_rope: bool = True):
         self.cfg = cfg
         self.device = torch.device(device)
         self.dtype = dtype
@@ -79,6 +82,15 @@ class RandomLlama:
         self.ln_final = ones.clone()
         self.inv_freq = 1.0 / (cfg.rope_theta ** (
             torch.arange(0, Dh, 2, device=self.device, dtype=torch.float32) / Dh))
+        # cosine / sine tables [rope_positions, Dh / 2]: the same fp32 products
+        # position * inv_freq as the per-step computation below, so the same bits
+        ang = torch.arange(cfg.rope_positions, device=self.device, dtype=torch.float32)[:, None] \
+            * self.inv_freq[None, :]
+        self.rope_cos, self.rope_sin = torch.cos(ang).contiguous(), torch.sin(ang).contiguous()
+        # with a backend that takes rope= (B200PagedBackend), q and k go to it
+        # unrotated and the rotation runs in its kernels (inside the decode
+        # launch for a decode step); otherwise torch rotates them here
+        self.fused_rope = fused_rope
         self.scale = Dh ** -0.5
 
     def param_bytes(self) -> int:
@@ -102,21 +114,28 @@ class RandomLlama:
         cfg = self.cfg
         T = tokens.shape[0]
         Hq, Hkv, Dh = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
-        pos = meta.positions.to(self.device).float()
-        ang = pos[:, None] * self.inv_freq[None, :]
-        cos, sin = torch.cos(ang)[:, None, :], torch.sin(ang)[:, None, :]
+        fused = self.fused_rope and hasattr(backend, "append_attend") and hasattr(backend, "rope")
+        if not fused:
+            pos = meta.positions.to(self.device).float()
+            ang = pos[:, None] * self.inv_freq[None, :]
+            cos, sin = torch.cos(ang)[:, None, :], torch.sin(ang)[:, None, :]
         x = self.embed[tokens.to(self.device).long()]
         for layer in range(cfg.n_layers):
             h = self._norm(x, self.ln_attn[layer])
             qkv = F.linear(h, self.w_qkv[layer])
-            q = self._rope(qkv[:, : Hq * Dh].view(T, Hq, Dh), cos, sin)
-            k = self._rope(qkv[:, Hq * Dh: (Hq + Hkv) * Dh].view(T, Hkv, Dh), cos, sin)
             v = qkv[:, (Hq + Hkv) * Dh:].reshape(T, Hkv, Dh)
-            if hasattr(backend, "append_attend"):  # one call (one launch for a decode step)
-                o = backend.append_attend(layer, k, v, q, self.scale, meta)
+            if fused:  # RoPE, KV-append and attention in the backend (one launch for a decode step)
+                q = qkv[:, : Hq * Dh].reshape(T, Hq, Dh)
+                k = qkv[:, Hq * Dh: (Hq + Hkv) * Dh].reshape(T, Hkv, Dh)
+                o = backend.append_attend(layer, k, v, q, self.scale, meta, rope=(self.rope_cos, self.rope_sin))
             else:
-                backend.append_kv(layer, k, v, meta)
-                o = backend.attend(q, layer, self.scale, meta)
+                q = self._rope(qkv[:, : Hq * Dh].view(T, Hq, Dh), cos, sin)
+                k = self._rope(qkv[:, Hq * Dh: (Hq + Hkv) * Dh].view(T, Hkv, Dh), cos, sin)
+                if hasattr(backend, "append_attend"):  # one call (one launch for a decode step)
+                    o = backend.append_attend(layer, k, v, q, self.scale, meta)
+                else:
+                    backend.append_kv(layer, k, v, meta)
+                    o = backend.attend(q, layer, self.scale, meta)
             x = x + F.linear(o.reshape(T, Hq * Dh), self.w_o[layer])
             h = self._norm(x, self.ln_ffn[layer])
             gu = F.linear(h, self.w_gate_up[layer])
