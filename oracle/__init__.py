@@ -23,5 +23,6 @@ from .paged_kv import (  # noqa: F401
     attend_reference,
     build_csr,
     last_page_len,
+    rope,
     slot_for,
 )

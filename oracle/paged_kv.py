@@ -24,6 +24,7 @@ __all__ = [
     "meta_arrays",
     "attend_reference",
     "attend_exact",
+    "rope",
     "OraclePool",
 ]
 
@@ -177,6 +178,31 @@ def attend_exact(
         p /= p.sum(axis=-1, keepdims=True)
         out[cu[i]: cu[i + 1]] = np.matmul(p, v).transpose(1, 0, 2)
     return out
+
+
+# ---------------------------------------------------------------------------
+# rotary embedding — the engine step before append_kv / attend
+# ---------------------------------------------------------------------------
+
+def rope(x: np.ndarray, positions, cos: np.ndarray, sin: np.ndarray) -> np.ndarray:
+    """Rotary embedding of ``x`` ``(tokens, heads, head_dim)`` at each token's
+    absolute position, with cosine / sine tables ``[max_pos, head_dim // 2]``.
+
+    The formula is the one of the reference's own paged model
+    (``tests/test_preemption.py:85-102``: the two halves a = x[..., :D/2],
+    b = x[..., D/2:] become ``a*cos - b*sin`` and ``a*sin + b*cos``) and of the
+    engine it stands in for, which indexes precomputed tables by
+    ``meta.positions`` (``docs/ENGINE_INTEGRATION.md:108``: ``cos[positions]``
+    applied to q and k). Arithmetic in the tables' dtype, every product and
+    sum rounded on its own (numpy evaluates each operation separately), then
+    cast to ``x``'s dtype (round to nearest even)."""
+    pos = np.asarray(positions, dtype=np.int64)
+    c = cos[pos][:, None, :]
+    s = sin[pos][:, None, :]
+    half = x.shape[-1] // 2
+    a = x[..., :half].astype(cos.dtype)
+    b = x[..., half:].astype(cos.dtype)
+    return np.concatenate([a * c - b * s, a * s + b * c], axis=-1).astype(x.dtype)
 
 
 # ---------------------------------------------------------------------------

@@ -174,6 +174,25 @@ def gen_batch(ref) -> None:
     print("batch_assembly: ok")
 
 
+def gen_rope(ref_root: str) -> None:
+    """The reference's own rotary embedding (``_rope`` of its paged-model tests,
+    tests/test_preemption.py:85-102, float64, theta 10000) on seeded inputs;
+    the positions include 0 and values past 2^11."""
+    import importlib.util
+
+    spec = importlib.util.spec_from_file_location("ref_test_preemption", Path(ref_root, "tests/test_preemption.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    g = torch.Generator().manual_seed(11)
+    T, H, D = 37, 3, 64
+    x = torch.randn(T, H, D, generator=g, dtype=torch.float64)
+    positions = torch.randint(0, 5000, (T,), generator=g, dtype=torch.int64)
+    positions[:3] = torch.tensor([0, 1, 4097])
+    out = mod._rope(x, positions)
+    np.savez(HERE / "rope.npz", x=x.numpy(), positions=positions.numpy(), out=out.numpy(), theta=10000.0)
+    print("rope: ok")
+
+
 def main() -> None:
     ref_root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("LLM_SERVING_LAYER_REF", "")
     if not ref_root or not Path(ref_root, "serving").is_dir():
@@ -184,6 +203,7 @@ def main() -> None:
     gen_copy(ref)
     gen_swap(ref)
     gen_batch(ref)
+    gen_rope(ref_root)
 
 
 if __name__ == "__main__":

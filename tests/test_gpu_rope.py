@@ -26,6 +26,7 @@ from helpers import FifoAllocator, Seq, meta_for, slots_meta
 from llm_serving_layer_b200 import B200PagedBackend
 from llm_serving_layer_b200._native import PkvError
 from llm_serving_layer_b200.llama import LlamaConfig, RandomLlama
+from oracle import rope as oracle_rope  # the checker
 
 pytestmark = pytest.mark.gpu
 
@@ -109,6 +110,10 @@ def test_rope_kernel_matches_the_fp32_formula_bitwise(dtype):
     bk.check_status()
     assert torch.equal(qo, torch_rope(q, pos, cos, sin))
     assert torch.equal(ko, torch_rope(k, pos, cos, sin))
+    if dtype == torch.float16:  # and the CPU oracle's restatement (numpy has no bf16)
+        c, s_, p = cos.cpu().numpy(), sin.cpu().numpy(), pos.cpu().numpy()
+        assert np.array_equal(qo.cpu().numpy(), oracle_rope(q.cpu().numpy(), p, c, s_))
+        assert np.array_equal(ko.cpu().numpy(), oracle_rope(k.cpu().numpy(), p, c, s_))
     # one tensor alone
     qo2, none = bk.rope(q, None, M, (cos, sin))
     assert none is None and torch.equal(qo2, qo)
@@ -141,6 +146,9 @@ def test_fused_decode_rope_equals_rope_then_append_attend(case, dtype):
     slots = m.slot_mapping.long()
     got = b.k_pool[1].reshape(-1, 8, 64)[slots]
     assert torch.equal(got, torch_rope(kn, m.positions, cos, sin))
+    if dtype == torch.float16:
+        want = oracle_rope(kn.cpu().numpy(), m.positions.cpu().numpy(), cos.cpu().numpy(), sin.cpu().numpy())
+        assert np.array_equal(got.cpu().numpy(), want)
 
 
 @pytest.mark.parametrize("qlens", [[37, 1, 200, 1, 5], [512], [1, 64, 1]])

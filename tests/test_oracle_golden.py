@@ -22,7 +22,7 @@ import pytest
 
 from cases import COPY_OPS, SWAP_GEOM, SWAP_TOKENS, attn_cases, copy_block_pool
 from llm_serving_layer_b200.meta import build_meta
-from oracle import OraclePool, attend_exact, attend_reference, build_csr, last_page_len, slot_for
+from oracle import OraclePool, attend_exact, attend_reference, build_csr, last_page_len, rope, slot_for
 
 GOLD = Path(__file__).resolve().parent / "golden"
 
@@ -236,3 +236,45 @@ def test_oracle_matches_live_reference(seed):
     want = bk.attend(torch.from_numpy(q), 0, 0.125, m).numpy().astype(np.float64)
     got = attend_reference(q, pool.k[0], pool.v[0], 0.125, m).astype(np.float64)
     assert np.all(np.abs(got - want) <= ulp_tol(want.astype(np.float16)))
+
+
+def test_oracle_rope_matches_reference_golden():
+    """``oracle.rope`` against the reference's own rotary embedding (``_rope``
+    of its paged-model tests, tests/test_preemption.py:85-102: float64, theta
+    10000), run by make_golden.py. The tables are recomputed here from the same
+    expression; numpy's and torch's pow / cos may differ in the last bit, which
+    an angle of a few thousand radians turns into ~1e-12, so the pin is 1e-9:
+    a wrong pairing, sign or position gives O(1) differences."""
+    g = np.load(GOLD / "rope.npz")
+    x, pos, out = g["x"], g["positions"], g["out"]
+    half = x.shape[-1] // 2
+    inv = float(g["theta"]) ** (-np.arange(half, dtype=np.float64) / half)
+    ang = np.arange(int(pos.max()) + 1, dtype=np.float64)[:, None] * inv[None, :]
+    got = rope(x, pos, np.cos(ang), np.sin(ang))
+    assert got.dtype == np.float64
+    np.testing.assert_allclose(got, out, rtol=0, atol=1e-9)
+    # a planted mistake is caught: rotating by position + 1
+    bad = rope(x, pos + 1, np.cos(np.vstack([ang, ang[-1:] + inv])), np.sin(np.vstack([ang, ang[-1:] + inv])))
+    assert np.abs(bad - out).max() > 1e-2
+
+
+def test_oracle_rope_float32_is_the_torch_formula_bit_for_bit():
+    """In float32 with fp16 data the oracle gives the bits of the formula as the
+    random-init Llama evaluates it with torch (each product rounded, then the
+    difference / sum, then fp16): the reference point of the CUDA kernels'
+    bit-exact RoPE tests."""
+    import torch
+
+    rs = np.random.RandomState(3)
+    x = (rs.standard_normal((50, 4, 64)) * 2).astype(np.float16)
+    pos = rs.randint(0, 2048, 50)
+    inv = 1.0 / (500000.0 ** (torch.arange(0, 64, 2, dtype=torch.float32) / 64))
+    ang = torch.arange(2048, dtype=torch.float32)[:, None] * inv[None, :]
+    cos, sin = torch.cos(ang), torch.sin(ang)
+    xt = torch.from_numpy(x)
+    c, s_ = cos[torch.from_numpy(pos)][:, None, :], sin[torch.from_numpy(pos)][:, None, :]
+    a, b = xt[..., :32].float(), xt[..., 32:].float()
+    want = torch.cat([a * c - b * s_, a * s_ + b * c], dim=-1).to(torch.float16).numpy()
+    got = rope(x, pos, cos.numpy(), sin.numpy())
+    assert got.dtype == np.float16
+    assert np.array_equal(got.view(np.uint16), want.view(np.uint16))
