@@ -203,6 +203,16 @@ PKV_API int pkv_append_attend_rope_planned(const pkv_pool* pool, int32_t layer, 
 PKV_API int pkv_attend_kernel(const pkv_pool* pool, int32_t n_heads, int32_t n_seqs, int32_t n_tokens,
                       int32_t decode_hint);
 
+/* A probe of the kernels' bounded waits (no counterpart in the reference,
+ * whose kernels are library calls): one warp waits on an mbarrier phase that
+ * nothing completes and then polls *never_set (a device int32 that must stay
+ * 0), each wait giving up after about 1 s as every wait in this library does;
+ * both set PKV_DEV_WAIT_TIMEOUT in *dev_status, and *result (if non-NULL)
+ * gets bit 0 / bit 1 set only if the barrier / the word were seen (0 when
+ * both waits ran out). About 2 s of one warp on `stream`; the context stays
+ * usable. For tests and health checks of a deployment. */
+PKV_API int pkv_wait_probe(const int32_t* never_set, int32_t* dev_status, int32_t* result, void* stream);
+
 /* Decode attention that allocates nothing and takes no workspace. No
  * counterpart in the reference: it is for callers that cannot allocate device
  * memory — a serving process that gives (nearly) all of HBM to its KV pool and
