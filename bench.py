@@ -1250,6 +1250,9 @@ def run_llama(torch, bk, args, device, rank) -> dict:
             "ms_per_step": round(dt * 1e3 / steps, 3), "forward_device_ms_per_step": round(fwd_ms, 3),
             "mean_batch_seqs": round(seqs / steps, 1),
             "mean_batch_tokens": round(toks / steps, 1),
+            "attention": ("B200PagedBackend.append_attend(..., rope=): RoPE, KV-append and attention in one "
+                          "launch per layer on decode steps; mixed steps: rotation kernel, append, prefill and "
+                          "decode kernels"),
             "timing": "host wall clock around the steps (host scheduling, batch assembly, H2D, forward, D2H)"}
 
 
