@@ -59,15 +59,26 @@ __global__ void __launch_bounds__(256) append_kernel(char* __restrict__ k_slab,
   if (warp >= 2 * n_tokens) return;
   const int64_t tok = warp >> 1;
   const int kv = int(warp & 1);
+  // The row's data does not depend on its slot: both loads are issued before
+  // either is used, so the kernel pays one memory round trip, not two in a row.
   const int64_t slot = slots[tok];
-  if (slot < 0 || slot >= n_slots) {
-    if (lane == 0 && kv == 0) flag(st, PKV_DEV_SLOT_OOB);
-    return;
-  }
   const T* src = reinterpret_cast<const T*>((kv ? v : k) + tok * row_bytes);
-  T* dst = reinterpret_cast<T*>((kv ? v_slab : k_slab) + slot * row_bytes);
   const int64_t n = row_bytes / W;
-  for (int64_t i = lane; i < n; i += 32) dst[i] = __ldg(src + i);
+  constexpr int U = 4;  // vectors per lane in flight
+  for (int64_t i0 = lane; i0 < n; i0 += 32 * U) {
+    T buf[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+      if (i0 + 32 * u < n) buf[u] = __ldg(src + i0 + 32 * u);
+    if (slot < 0 || slot >= n_slots) {
+      if (lane == 0 && kv == 0) flag(st, PKV_DEV_SLOT_OOB);
+      return;
+    }
+    T* dst = reinterpret_cast<T*>((kv ? v_slab : k_slab) + slot * row_bytes);
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+      if (i0 + 32 * u < n) dst[i0 + 32 * u] = buf[u];
+  }
 }
 
 // ------------------------------------------------------------------ copy blocks
