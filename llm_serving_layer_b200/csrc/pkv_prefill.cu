@@ -159,6 +159,9 @@ __global__ void __launch_bounds__(1024) prefill_plan_kernel(
     }
   }
   if (tid == 0) *n_tiles = s_total;
+  // the tcgen05 prefill kernel reads the tile list before its griddepcontrol.wait
+  // (it starts only once this kernel has completed): stores visible at GPU scope
+  __threadfence();
   if (!mixed) return;
 
   // ---- decode rows of the mixed batch, listed in sequence order

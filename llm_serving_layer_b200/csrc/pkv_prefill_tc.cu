@@ -69,6 +69,7 @@ struct TcArgs {
   int64_t total_pages;
   int n_seqs, n_tokens, n_heads, n_kv, layer;
   float scale_log2;
+  int early_ctas;  // CTAs [0, early_ctas) are the first wave: they read the plan before griddepcontrol.wait
 };
 
 // ---------------------------------------------------------------- tcgen05 helpers
@@ -205,32 +206,54 @@ __global__ void __launch_bounds__(TC_THREADS, 2) prefill_tc_kernel(const __grid_
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tile_idx = int(blockIdx.x) / a.n_kv, h = int(blockIdx.x) % a.n_kv;
   pdl_trigger();
-  pdl_wait();  // the plan, q and this step's append are written by earlier kernels
-  if (tile_idx >= *a.n_tiles) return;
-  const int2 tile = a.tiles[tile_idx];
+  // A CTA of the first wave may start while the kernel before it (this
+  // layer's append, the previous layer's attention) still runs: up to
+  // pdl_wait() it reads only the plan's tile list and the step's BatchMeta,
+  // both written before the plan kernel completed (that kernel lets nothing
+  // start before then and fences its stores), through L2 (ld.global.cg: no line
+  // this SM cached earlier), and checks the tile's page ids. Later CTAs find
+  // the earlier kernels long finished: they wait first and read through L1,
+  // where the CTAs of one sequence share the lines.
+  const bool early = int(blockIdx.x) < a.early_ctas;  // uniform over the CTA
+  if (!early) pdl_wait();
+  auto ld = [&](const int32_t* p) -> int32_t { return early ? __ldcg(p) : *p; };
+  if (tile_idx >= ld(a.n_tiles)) return;
+  const int2 tile = early ? __ldcg(a.tiles + tile_idx) : a.tiles[tile_idx];
   const int s = tile.x, j0 = tile.y;
   bool bad = s < 0 || s >= a.n_seqs;
   int q0 = 0, ql = 0, lpl = 0;
   int64_t pa = 0, pb = 0;
   if (!bad) {
-    q0 = a.cu_q[s];
-    ql = a.cu_q[s + 1] - q0;
-    pa = a.kv_indptr[s];
-    pb = a.kv_indptr[s + 1];
-    lpl = a.last_page_len[s];
+    q0 = ld(a.cu_q + s);
+    ql = ld(a.cu_q + s + 1) - q0;
+    pa = ld(a.kv_indptr + s);
+    pb = ld(a.kv_indptr + s + 1);
+    lpl = ld(a.last_page_len + s);
   }
   const int64_t npages64 = pb - pa;
   const int64_t kv64 = (npages64 - 1) * TC_P + lpl;
   bad = bad || npages64 < 1 || pa < 0 || pb > a.total_pages || lpl < 1 || lpl > TC_P || ql < 1 ||
         j0 < 0 || j0 >= ql || kv64 < ql || kv64 >= 0x7fffffff || q0 < 0 || q0 + ql > a.n_tokens;
-  if (!bad && a.kv_lens && a.kv_lens[s] != kv64) bad = true;
+  if (!bad && a.kv_lens && ld(a.kv_lens + s) != kv64) bad = true;
   const int kv = bad ? 0 : int(kv64);
   const int npages = bad ? 0 : int(npages64);
   const int n_pg = bad ? 0 : tc_tile_pages(kv, ql, j0, TPT);  // pages with keys visible to the tile
   const int nblk = (n_pg + TC_PPB - 1) / TC_PPB;
+  auto check_pages = [&]() {
+    if (threadIdx.x == 0) s_bad = bad ? 1 : 0;
+    __syncthreads();
+    for (int i = threadIdx.x; i < n_pg; i += blockDim.x) {
+      const int id = ld(a.kv_indices + pa + i);
+      if (id < 0 || id >= a.num_blocks) s_bad = 2;
+    }
+  };
+  if (early) {
+    check_pages();
+    pdl_wait();  // q and this layer's appended rows are written by earlier kernels
+  }
   // The softmax threads' query rows, loaded now so the loads travel while the
-  // page ids are checked and the barriers and tensor memory are set up; they
-  // are stored to shared memory (swizzled) further down.
+  // page ids are checked (later CTAs) and the barriers and tensor memory are
+  // set up; they are stored to shared memory (swizzled) further down.
   const int r_sm = (warp & 3) * 32 + lane;  // a softmax thread's row
   const int jq_sm = j0 + r_sm % TPT;
   uint4 qv[8];
@@ -241,12 +264,7 @@ __global__ void __launch_bounds__(TC_THREADS, 2) prefill_tc_kernel(const __grid_
 #pragma unroll
     for (int c = 0; c < 8; ++c) qv[c] = qok ? __ldg(src + c) : make_uint4(0u, 0u, 0u, 0u);
   }
-  if (threadIdx.x == 0) s_bad = bad ? 1 : 0;
-  __syncthreads();
-  for (int i = threadIdx.x; i < n_pg; i += blockDim.x) {
-    const int id = a.kv_indices[pa + i];
-    if (id < 0 || id >= a.num_blocks) s_bad = 2;
-  }
+  if (!early) check_pages();
   if (threadIdx.x == 0) {
     prefetch_tmap(&tmap);
     for (int i = 0; i < TC_NST; ++i) {
@@ -570,6 +588,7 @@ int prefill_tc_attend(const pkv_pool& p, int layer, int n_heads, const void* q, 
   a.n_kv = p.n_kv_heads;
   a.layer = layer;
   a.scale_log2 = scale * 1.4426950408889634f;
+  a.early_ctas = 2 * num_sms();  // two CTAs per SM (__launch_bounds__ and shared memory)
   const int qt = prefill_tc_tile_tokens(n_heads, p.n_kv_heads);
   const int64_t bound = std::min<int64_t>((int64_t(b.n_tokens) + qt - 1) / qt + b.n_seqs, tiles_cap);
   const int64_t grid = std::max<int64_t>(1, bound) * p.n_kv_heads;
