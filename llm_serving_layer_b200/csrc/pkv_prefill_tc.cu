@@ -249,6 +249,16 @@ __global__ void __launch_bounds__(TC_THREADS, 2) prefill_tc_kernel(const __grid_
   };
   if (early) {
     check_pages();
+    // warm L2 with this head's slices of the tile's first two key blocks: a
+    // hint only (the loads after the wait read through L2, where this layer's
+    // appended rows land too), so it may run before the wait
+    if (warp == 0 && lane < min(n_pg, 2 * TC_PPB)) {
+      const int id = __ldcg(a.kv_indices + pa + lane);
+      if (id >= 0 && id < a.num_blocks) {
+        tma_prefetch_l2_4d(&tmap, 0, id * TC_P, h, 2 * a.layer);
+        tma_prefetch_l2_4d(&tmap, 0, id * TC_P, h, 2 * a.layer + 1);
+      }
+    }
     pdl_wait();  // q and this layer's appended rows are written by earlier kernels
   }
   // The softmax threads' query rows, loaded now so the loads travel while the
