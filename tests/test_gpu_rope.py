@@ -229,3 +229,47 @@ def test_llama_with_fused_rope_gives_the_same_logits_as_torch_rope():
         assert torch.equal(logits[0], logits[1]), f"step {n}"
         assert bks[0].last_kernel == ("prefill" if n == 0 else "decode")
     assert torch.equal(bks[0]._pool, bks[1]._pool)
+
+
+def test_rope_on_a_geometry_without_the_fused_launch():
+    """head_dim 128 (the generic attention kernel; the decode kernel takes 64):
+    the rotation kernel handles any even head_dim, and a decode step with
+    rope= falls back to rotating first and the plain call, with the same
+    result as doing that by hand."""
+    D, Hkv, Hq = 128, 2, 8
+    cos, sin = tables(max_pos=512, D=D)
+    rs = np.random.RandomState(6)
+    bks = []
+    for _ in range(2):
+        bk = B200PagedBackend(1, 64, 16, Hkv, Hq, D, device=DEV, dtype=torch.float16)
+        bk._pool.fill_(3.0)
+        bks.append(bk)
+    alloc = FifoAllocator(64, 16, order=rs.permutation(64))
+    seqs = []
+    for i, c in enumerate([40, 7, 100]):
+        s = Seq(alloc, i)
+        s.append(c - 1)
+        seqs.append(s)
+    hist = np.concatenate([[s.slot_for(p) for p in range(s.num_tokens)] for s in seqs]).astype(np.int64)
+    g = torch.Generator(device=DEV).manual_seed(6)
+    k = (torch.randn(hist.size, Hkv, D, generator=g, device=DEV) * 0.7).half()
+    v = (torch.randn(hist.size, Hkv, D, generator=g, device=DEV) * 0.7).half()
+    for bk in bks:
+        bk.append_kv(0, k, v, slots_meta(hist))
+    for s in seqs:
+        s.append(1)
+    m = meta_for(seqs, [1, 1, 1], device=DEV)
+    kn = (torch.randn(3, Hkv, D, generator=g, device=DEV) * 0.7).half()
+    vn = (torch.randn(3, Hkv, D, generator=g, device=DEV) * 0.7).half()
+    q = torch.randn(3, Hq, D, generator=g, device=DEV).half()
+    a, b = bks
+    qr, kr = a.rope(q, kn, m, (cos, sin))
+    want = oracle_rope(q.cpu().numpy(), m.positions.cpu().numpy(), cos.cpu().numpy(), sin.cpu().numpy())
+    assert np.array_equal(qr.cpu().numpy(), want)
+    out_a = a.append_attend(0, kr, vn, qr, 0.125, m)
+    out_b = b.append_attend(0, kn, vn, q, 0.125, m, rope=(cos, sin))
+    torch.cuda.synchronize()
+    a.check_status()
+    b.check_status()
+    assert torch.equal(out_a, out_b)
+    assert torch.equal(a._pool, b._pool)
