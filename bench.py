@@ -1,6 +1,6 @@
 """
 Benchmark of the paged-KV hot path on B200: paged decode attention over all 16
-layers of Llama-3.2-1B geometry at batch 256.
+layers of Llama-3.2-1B geometry at batch 256 (config 2: the headline workload).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
 
