@@ -1333,6 +1333,71 @@ def run_llama(torch, bk, args, device, rank, feed="device", record=0) -> dict:
             "timing": "host wall clock around the steps (host scheduling, batch assembly, H2D, forward, D2H)"}
 
 
+def decode_sweep() -> None:
+    """The decode kernel against batch size: for 64-2048 sequences with config
+    2's context distribution (scattered pages of a pool sized for the largest
+    batch), one graph of the 16 layers' decode launches back to back, replayed
+    20 times after 3 warm-up replays; per launch, the mean time and the
+    algorithmic bytes (K and V rows, q and out, page descriptors) over it as a
+    fraction of the measured HBM peak. The 16 layers' K/V (≥ 0.5 GB per replay
+    at 64 sequences) exceed L2. One JSON line per batch size."""
+    import torch
+
+    from llm_serving_layer_b200 import B200PagedBackend
+    from llm_serving_layer_b200.meta import build_meta
+
+    dev = torch.device("cuda", 0)
+    sizes = (64, 128, 256, 512, 1024, 2048)
+    rs = np.random.RandomState(2026)
+    ctxs = {n: contexts(rs, n) for n in sizes}
+    nb = int(max(((c + P - 1) // P).sum() for c in ctxs.values())) + 64
+    bk = B200PagedBackend(L, nb, P, HKV, HQ, D, device=dev, dtype=torch.float16, validate="device")
+    g = torch.Generator(device=dev).manual_seed(7)
+    for layer in range(L):
+        for kv in range(2):
+            bk._pool[layer, kv].normal_(0.0, KV_STD, generator=g)
+    peak, peak_kind = measured_peaks()
+    for n in sizes:
+        ctx = ctxs[n]
+        perm = rs.permutation(nb)
+        tables, o = [], 0
+        for c in ctx:
+            k = int((c + P - 1) // P)
+            tables.append(perm[o:o + k].tolist())
+            o += k
+        m = build_meta(tables, ctx, [1] * n, P, device=dev)
+        q = torch.randn((n, HQ, D), generator=g, device=dev).half()
+        out = torch.empty_like(q)
+        bk.invalidate_plan()
+        bk.reserve_workspace(n, o)
+        bk.plan(m)
+        for layer in range(L):
+            bk.attend(q, layer, SCALE, m, out=out)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for layer in range(L):
+                bk.attend(q, layer, SCALE, m, out=out)
+        for _ in range(3):
+            graph.replay()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(20):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        bk.check_status()
+        us = e0.elapsed_time(e1) * 1e3 / (20 * L)
+        alg = int(ctx.sum()) * HKV * D * 2 * 2 + n * HQ * D * 2 * 2 + o * 8
+        print(json.dumps({"decode_sweep": {"n_seqs": n, "pages": o, "avg_launch_us": round(us, 2),
+                                           "alg_bytes_per_launch": alg,
+                                           "achieved_gbs": round(alg / us / 1e3, 1), "peak_gbs": peak,
+                                           "peak_kind": peak_kind, "frac": round(alg / us / 1e3 / peak, 4)}}),
+              flush=True)
+        del graph
+
+
 def kvops_probe() -> None:
     """A small fixed workload of the KV-append, copy-on-write and swap kernels
     for kernel profilers (ncu): on a 16-layer, 8000-block (4 GB) pool,
@@ -1404,9 +1469,14 @@ def main() -> None:
     ap.add_argument("--llama-steps", type=int, default=100)
     ap.add_argument("--kvops-probe", action="store_true",
                     help="run only the small append / copy-on-write / swap workload (for kernel profilers)")
+    ap.add_argument("--decode-sweep", action="store_true",
+                    help="run only the decode kernel over batch sizes 64-2048 (one JSON line per size)")
     args = ap.parse_args()
     if args.kvops_probe:
         kvops_probe()
+        return
+    if args.decode_sweep:
+        decode_sweep()
         return
     args.warmup = max(3, args.warmup)
     if args.impl == "reference":
