@@ -235,13 +235,33 @@ PKV_API int pkv_attend_decode_noalloc(const pkv_pool* pool, int32_t layer, int32
                                       const void* q, void* out, float scale,
                                       const pkv_batch* batch, void* stream);
 
+/* ---- greedy sampling --------------------------------------------------------
+ * Replaces the scheduler's torch.argmax(logits, dim=-1) after each forward pass
+ * (serving/scheduler/scheduler.py:756-757); its .tolist() host read becomes the
+ * caller's asynchronous copy of `sampled`, which can be read a step later.
+ * For each of n_rows rows of `logits` (dtype PKV_F16 / PKV_BF16 / PKV_F32,
+ * row r at logits + r * row_stride elements, `vocab` entries): the index of the
+ * row maximum, the FIRST such index on ties, a NaN counting as larger than every
+ * number (torch.argmax's result). The token is written to sampled[r] (int64,
+ * if `sampled` is non-NULL) and to the token table: tokens[rows[r]] when `rows`
+ * (int32 [n_rows]) is given — rows[r] < 0 skips the row, rows[r] >= tokens_len
+ * skips it and sets PKV_DEV_SLOT_OOB in *dev_status — else tokens[r]. One launch
+ * on `stream`; no workspace. */
+PKV_API int pkv_sample_greedy(int32_t dtype, const void* logits, int64_t n_rows, int64_t vocab,
+                              int64_t row_stride, const int32_t* rows, int64_t* tokens, int64_t tokens_len,
+                              int64_t* sampled, int32_t* dev_status, void* stream);
+
 /* ---- copy-on-write ---------------------------------------------------------
  * Replaces PagedTorchBackend.copy_block (serving/backends/paged_torch.py:181-207)
  * and FlashInferBackend.copy_block (flashinfer_backend.py:415-441), batched:
  * for every pair i, block dst[i] := block src[i] in every layer, K and V, in one
  * launch. src/dst: device int32 [n_pairs]. Pairs with src == dst are no-ops.
- * The dst set must not intersect the src set (checked by the host wrapper);
- * ids outside the pool are skipped and flagged PKV_DEV_SLOT_OOB. */
+ * This function does NOT check that the destinations are distinct or that the
+ * dst set is disjoint from the src set: the pairs run concurrently, so a chain
+ * (a->b with b->c) or a repeated destination gives an order-dependent result.
+ * The caller guarantees both (the Python wrapper B200PagedBackend.copy_blocks
+ * checks them on the host before calling). Ids outside the pool are skipped and
+ * flagged PKV_DEV_SLOT_OOB. */
 PKV_API int pkv_copy_blocks(const pkv_pool* pool, const int32_t* src, const int32_t* dst,
                     int64_t n_pairs, int32_t* dev_status, void* stream);
 

@@ -41,17 +41,6 @@ def test_library_exports_every_declared_symbol(lib):
     assert lib.pkv_version() >= 100
 
 
-def test_every_entry_point_is_listed_in_the_integration_guide():
-    """Each C entry point has a row in the integration guide's table, with the
-    reference interface it replaces (or why it has none)."""
-    guide = (HEADER.parents[1] / "INTEGRATION.md").read_text()
-    rows = [line for line in guide.splitlines() if line.startswith("| `pkv_")]
-    listed = set(re.findall(r"`(pkv_\w+?)\*?`", "\n".join(rows)))
-    for name in declared_symbols():
-        assert name in listed or any(name.startswith(p) for p in listed if p.endswith("_")), \
-            f"{name} has no row in the integration guide"
-
-
 def test_argument_errors_are_reported_without_a_device(lib):
     assert lib.pkv_append_kv(None, 0, None, None, None, 1, None, None) == N.PKV_ERR_ARG
     assert b"NULL" in lib.pkv_last_error()

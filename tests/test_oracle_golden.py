@@ -187,11 +187,12 @@ def test_oracle_detects_a_wrong_gqa_mapping():
     assert np.abs(bad - good).max() > 1e-2
 
 
-REF = os.environ.get("LLM_SERVING_LAYER_REF", "/root/reference")
+REF = os.environ.get("LLM_SERVING_LAYER_REF", "")
 
 
-@pytest.mark.skipif(not Path(REF, "serving", "backends", "paged_torch.py").is_file(),
-                    reason="reference checkout not present (fixtures still pin the oracle)")
+@pytest.mark.skipif(not REF or not Path(REF, "serving", "backends", "paged_torch.py").is_file(),
+                    reason="set LLM_SERVING_LAYER_REF to a reference checkout to compare against it live "
+                           "(the committed fixtures pin the oracle without it)")
 @pytest.mark.parametrize("seed", [0, 1, 2])
 def test_oracle_matches_live_reference(seed):
     """Fresh seeded ragged batches: oracle vs the reference's PagedTorchBackend."""
