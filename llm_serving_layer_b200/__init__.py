@@ -12,7 +12,10 @@ Drop-ins behind the reference's own interfaces:
 * ``BatchMeta`` / ``build_meta`` — the engine's step descriptor (field-for-field)
   and a vectorised host assembler;
 * ``DeviceBlockTables`` — block tables kept on the device and each step's
-  ``BatchMeta`` assembled there, replacing the engine's ``build_batch_meta``.
+  ``BatchMeta`` assembled there, replacing the engine's ``build_batch_meta``;
+* ``sample_greedy`` / ``TokenReadback`` — greedy sampling on the device into a
+  device token table, with the host reading the tokens a step later,
+  replacing the scheduler's ``torch.argmax(logits).tolist()``.
 
 All compute runs in ``_lib/libpkv.so`` (hand-written CUDA, C ABI in
 ``include/pkv.h``); build it with ``python -m llm_serving_layer_b200.build``.
@@ -20,6 +23,7 @@ All compute runs in ``_lib/libpkv.so`` (hand-written CUDA, C ABI in
 
 from .backend import B200PagedBackend
 from .meta import AttentionBackend, BatchMeta, build_meta
+from .sampling import TokenReadback, sample_greedy
 from .swap import B200SwapSpace, SwapHandle, SwapSpaceFull
 from .tables import DeviceBlockTables
 
@@ -32,4 +36,6 @@ __all__ = [
     "AttentionBackend",
     "build_meta",
     "DeviceBlockTables",
+    "sample_greedy",
+    "TokenReadback",
 ]

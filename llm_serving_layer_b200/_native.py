@@ -74,6 +74,7 @@ SIGNATURES = {
                                                c_i32, c_vp, c_size, c_vp, c_vp, c_vp, c_i64, c_vp]),
     "pkv_attend_decode_noalloc": (c_i32, [P_POOL, c_i32, c_i32, c_vp, c_vp, c_float, P_BATCH, c_vp]),
     "pkv_wait_probe": (c_i32, [c_vp, c_vp, c_vp, c_vp]),
+    "pkv_sample_greedy": (c_i32, [c_i32, c_vp, c_i64, c_i64, c_i64, c_vp, c_vp, c_i64, c_vp, c_vp, c_vp]),
     "pkv_copy_blocks": (c_i32, [P_POOL, c_vp, c_vp, c_i64, c_vp, c_vp]),
     "pkv_copy_block": (c_i32, [P_POOL, c_i64, c_i64, c_vp]),
     "pkv_build_batch_meta": (c_i32, [P_TABLES, c_vp, c_vp, c_i32, c_i32, P_META_OUT, c_vp, c_vp]),
