@@ -166,6 +166,27 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
+def decode_traffic(alg_bytes: float) -> tuple[int | None, str]:
+    """DRAM bytes of one decode launch: the ncu capture's DRAM bytes per
+    algorithmic byte (profiles/decode_traffic.json) times this launch's
+    algorithmic bytes — only while the decode kernel's sources hash to what the
+    capture ran; otherwise None (stale)."""
+    import hashlib
+
+    tfile = ROOT / "profiles" / "decode_traffic.json"
+    try:
+        tj = json.loads(tfile.read_text())
+        h = hashlib.sha256()
+        for f in tj["source_files"]:
+            h.update((ROOT / f).read_bytes())
+        if h.hexdigest() != tj["source_sha256"]:
+            return None, "stale: the decode kernel's sources changed since the ncu capture"
+        return (round(float(tj["dram_bytes_per_alg_byte"]) * alg_bytes),
+                f"ncu capture ({tj['capture']}): DRAM bytes per algorithmic byte x this launch's algorithmic bytes")
+    except Exception as e:  # noqa: BLE001
+        return None, f"unavailable ({type(e).__name__})"
+
+
 def measured_peaks() -> tuple[float, str]:
     p = ROOT / "MEASURED_PEAKS.json"
     try:
@@ -190,42 +211,180 @@ def cpu_threads() -> int:
 # ------------------------------------------------------------------ CPU oracle timing
 
 
-def cpu_oracle_step_time(seed: int, budget_s: float = 10.0) -> dict:
-    """Time the CPU oracle (the reference's append_kv + attend restated in numpy,
-    float32 — CPU half-precision matmul has no BLAS path) on one layer of the
-    full 256-sequence batch, repeated for ~budget_s; returns seconds per layer."""
-    from oracle import OraclePool, attend_reference  # CPU baseline leg only
-    from llm_serving_layer_b200.meta import build_meta
+class CpuDecodeStep:
+    """The CPU oracle (the reference's append_kv + attend restated in numpy,
+    float32 — CPU half-precision matmul has no BLAS path) on config 2: all 16
+    layers of the 256-sequence batch, each layer with its own pool slab, one new
+    token per sequence per step."""
+
+    def __init__(self, seed: int, max_steps: int):
+        from oracle import OraclePool  # CPU baseline / reference arm only
+
+        rs = np.random.RandomState(seed)
+        self.ctx = contexts(rs)
+        pages = (self.ctx + max_steps + P - 1) // P
+        nb = int(pages.sum())
+        perm = rs.permutation(nb)
+        self.tables, o = [], 0
+        for pg in pages:
+            self.tables.append(perm[o:o + pg].tolist())
+            o += pg
+        self.pool = OraclePool(L, nb, P, HKV, D, dtype=np.float32)
+        base_k = (rs.standard_normal(self.pool.k[0].shape) * KV_STD).astype(np.float32)
+        base_v = (rs.standard_normal(self.pool.v[0].shape) * KV_STD).astype(np.float32)
+        for layer in range(L):  # every layer its own slab (same values: the timing does not depend on them)
+            np.copyto(self.pool.k[layer], base_k)
+            np.copyto(self.pool.v[layer], base_v)
+        self.q = [rs.standard_normal((N_SEQ, HQ, D)).astype(np.float32) for _ in range(L)]
+        self.kn = [(rs.standard_normal((N_SEQ, HKV, D)) * KV_STD).astype(np.float32) for _ in range(L)]
+        self.vn = [(rs.standard_normal((N_SEQ, HKV, D)) * KV_STD).astype(np.float32) for _ in range(L)]
+
+    def meta(self, s: int):
+        from llm_serving_layer_b200.meta import build_meta
+
+        return build_meta(self.tables, self.ctx + s + 1, [1] * N_SEQ, P)
+
+    def step(self, m) -> float:
+        """One 16-layer step (append_kv then attend per layer); seconds."""
+        from oracle import attend_reference
+
+        slots = m.slot_mapping.numpy()
+        t0 = time.perf_counter()
+        for layer in range(L):
+            self.pool.append_kv(layer, self.kn[layer], self.vn[layer], slots)
+            attend_reference(self.q[layer], self.pool.k[layer], self.pool.v[layer], SCALE, m)
+        return time.perf_counter() - t0
+
+
+def cpu_decode_rate(seed: int, budget_s: float = 10.0) -> dict:
+    """Whole 16-layer steps of the CPU oracle for about ``budget_s`` (at least 2)."""
+    est = 2 + int(budget_s)  # steps never exceed ~1 s each on a many-core host
+    cs = CpuDecodeStep(seed, est + 64)
+    times = []
+    t_end = time.perf_counter() + budget_s
+    s = 0
+    while True:
+        times.append(cs.step(cs.meta(s)))
+        s += 1
+        if (time.perf_counter() > t_end and len(times) >= 2) or s >= est + 64:
+            break
+    return {"step_s": sum(times) / len(times), "steps": len(times), "cores": cpu_threads(),
+            "sum_ctx": int(cs.ctx.sum())}
+
+
+def cpu_swap_rate(seed: int, budget_s: float = 5.0) -> dict:
+    """Config 4's swap algorithm on CPU arrays (the reference's KVSwapSpace
+    restated: per-layer gather of a sequence's blocks into (L, nb, 16, 8, 64) K
+    and V buffers, and the scatter back into fresh blocks), fp16, over a sample
+    of the 64 victims."""
+    from oracle import OraclePool
 
     rs = np.random.RandomState(seed)
-    ctx = contexts(rs)
-    pages = (ctx + P - 1) // P
+    nb_seq, n_vict = 64, 16
+    nb_pool = 2 * nb_seq * n_vict + 256
+    pool = OraclePool(L, nb_pool, P, HKV, D, dtype=np.float16)
+    for layer in range(L):
+        pool.k[layer].fill(1)  # touch every page
+        pool.v[layer].fill(1)
+    perm = rs.permutation(nb_pool)
+    victims = [perm[i * nb_seq:(i + 1) * nb_seq] for i in range(n_vict)]
+    fresh = [perm[(n_vict + i) * nb_seq:(n_vict + i + 1) * nb_seq] for i in range(n_vict)]
+    per_dir = 2 * L * nb_seq * P * HKV * D * 2  # bytes one swap moves one way (K and V, all layers)
+    t_out = t_in = 0.0
+    n = 0
+    t_end = time.perf_counter() + budget_s
+    while n < 4 * n_vict and (n < n_vict or time.perf_counter() < t_end):
+        i = n % n_vict
+        t0 = time.perf_counter()
+        k, v = pool.swap_out(victims[i])
+        t1 = time.perf_counter()
+        pool.swap_in(k, v, fresh[i])
+        t_in += time.perf_counter() - t1
+        t_out += t1 - t0
+        n += 1
+    return {"d2h_gbs": round(n * per_dir / t_out / 1e9, 2), "h2d_gbs": round(n * per_dir / t_in / 1e9, 2),
+            "swaps": n, "cores": 1,
+            "sample": (f"{n} swap-outs and swap-ins of 1024-token victims ({per_dir / 2**20:.0f} MiB each way), "
+                       "numpy fancy-index gather/scatter over a 16-layer fp16 host pool (the reference's "
+                       "KVSwapSpace on CPU tensors, restated); GB/s per direction")}
+
+
+def cpu_llama_rate(seed: int, budget_s: float = 10.0, n_seqs: int = 16) -> dict:
+    """Config 5's decode step on the host cores at reduced scale: Llama-3.2-1B
+    geometry (hidden 2048, 16 layers, 32/8 heads of 64, SwiGLU 8192, vocab
+    128256, RoPE theta 500000, RMSNorm) in float32 numpy, random weights,
+    ``n_seqs`` sequences with config 2's context distribution; each step
+    appends one token per sequence, attends through the oracle (the
+    reference's PagedTorchBackend arithmetic restated), and takes the greedy
+    argmax of the logits."""
+    from oracle import OraclePool, attend_reference, rope
+
+    from llm_serving_layer_b200.meta import build_meta
+
+    H, FF, V = 2048, 8192, 128256
+    rs = np.random.RandomState(seed)
+    rng = np.random.default_rng(seed)
+
+    def w(*shape):
+        return (rng.random(shape, dtype=np.float32) - 0.5) * (2.0 / math.sqrt(shape[0]))
+
+    emb = np.empty((V, H), dtype=np.float32)  # random rows, a 1024-row template repeated
+    tmpl_rows = w(1024, H)
+    for r0 in range(0, V, 1024):
+        emb[r0:r0 + 1024] = tmpl_rows[:min(1024, V - r0)]
+    tmpl = {"qkv": w(H, (HQ + 2 * HKV) * D), "o": w(HQ * D, H), "gu": w(H, 2 * FF), "dn": w(FF, H)}
+    layers = [{k: v.copy() for k, v in tmpl.items()} for _ in range(L)]  # every layer its own weights
+    ctx = contexts(rs, n_seqs)
+    max_steps = 256
+    pages = (ctx + max_steps + P - 1) // P
     nb = int(pages.sum())
     perm = rs.permutation(nb)
     tables, o = [], 0
-    for p in pages:
-        tables.append(perm[o:o + p].tolist())
-        o += p
-    pool = OraclePool(1, nb, P, HKV, D, dtype=np.float32)
-    pool.k[0][:] = (rs.standard_normal(pool.k[0].shape) * KV_STD).astype(np.float32)
-    pool.v[0][:] = (rs.standard_normal(pool.v[0].shape) * KV_STD).astype(np.float32)
-    m = build_meta(tables, ctx, [1] * N_SEQ, P)
-    slots = m.slot_mapping.numpy()
-    q = rs.standard_normal((N_SEQ, HQ, D)).astype(np.float32)
-    kn = (rs.standard_normal((N_SEQ, HKV, D)) * KV_STD).astype(np.float32)
-    vn = (rs.standard_normal((N_SEQ, HKV, D)) * KV_STD).astype(np.float32)
+    for pg in pages:
+        tables.append(perm[o:o + pg].tolist())
+        o += pg
+    pool = OraclePool(L, nb, P, HKV, D, dtype=np.float32)
+    for layer in range(L):
+        pool.k[layer][:] = (rs.standard_normal(pool.k[layer].shape) * KV_STD).astype(np.float32) if layer == 0 \
+            else pool.k[0]
+        pool.v[layer][:] = pool.k[layer]
+    inv = 1.0 / (500000.0 ** (np.arange(0, D, 2, dtype=np.float32) / D))
+    ang = np.arange(2048 + max_steps, dtype=np.float32)[:, None] * inv[None, :]
+    cos, sin = np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
+    toks = rs.randint(0, V, size=n_seqs)
+
+    def norm(x):
+        return x / np.sqrt(np.mean(x * x, axis=-1, keepdims=True) + 1e-5)
+
     times = []
     t_end = time.perf_counter() + budget_s
-    while True:
+    s = 0
+    while s < max_steps and (len(times) < 2 or time.perf_counter() < t_end):
+        m = build_meta(tables, ctx + s + 1, [1] * n_seqs, P)
+        pos, slots = m.positions.numpy(), m.slot_mapping.numpy()
         t0 = time.perf_counter()
-        pool.append_kv(0, kn, vn, slots)
-        attend_reference(q, pool.k[0], pool.v[0], SCALE, m)
+        x = emb[toks]
+        for layer in range(L):
+            wl = layers[layer]
+            qkv = norm(x) @ wl["qkv"]
+            q = rope(qkv[:, :HQ * D].reshape(n_seqs, HQ, D), pos, cos, sin)
+            k = rope(qkv[:, HQ * D:(HQ + HKV) * D].reshape(n_seqs, HKV, D), pos, cos, sin)
+            v = qkv[:, (HQ + HKV) * D:].reshape(n_seqs, HKV, D)
+            pool.append_kv(layer, k, v, slots)
+            a = attend_reference(q, pool.k[layer], pool.v[layer], SCALE, m)
+            x = x + a.reshape(n_seqs, HQ * D) @ wl["o"]
+            gu = norm(x) @ wl["gu"]
+            g, u = gu[:, :FF], gu[:, FF:]
+            x = x + ((g / (1.0 + np.exp(-g))) * u) @ wl["dn"]
+        toks = np.argmax(norm(x) @ emb.T, axis=-1)
         times.append(time.perf_counter() - t0)
-        if time.perf_counter() > t_end and len(times) >= 2:
-            break
-    per_layer = statistics.median(times)
-    return {"per_layer_s": per_layer, "iters": len(times), "cores": cpu_threads(),
-            "sum_ctx": int(ctx.sum())}
+        s += 1
+    step_s = sum(times) / len(times)
+    return {"generated_tok_per_s": round(n_seqs / step_s, 2), "ms_per_step": round(step_s * 1e3, 1),
+            "steps": len(times), "cores": cpu_threads(),
+            "sample": (f"{len(times)} decode steps of {n_seqs} sequences (config 5 runs 1024 per GPU), "
+                       "Llama-3.2-1B geometry in float32 numpy with random weights, attention through the "
+                       "oracle's restatement of PagedTorchBackend, greedy argmax; host wall clock")}
 
 
 # ------------------------------------------------------------------ reference arm
@@ -236,48 +395,32 @@ def run_reference(args) -> None:
     if rank != 0:
         return
     steps, warmup = args.steps_ref, args.warmup
-    from oracle import OraclePool, attend_reference  # the reference arm times the oracle port
-    from llm_serving_layer_b200.meta import build_meta
-
-    rs = np.random.RandomState(args.seed)
-    ctx = contexts(rs)
-    pages = (ctx + steps + warmup + P - 1) // P
-    nb = int(pages.sum())
-    perm = rs.permutation(nb)
-    tables, o = [], 0
-    for p in pages:
-        tables.append(perm[o:o + p].tolist())
-        o += p
-    pool = OraclePool(1, nb, P, HKV, D, dtype=np.float32)
-    pool.k[0][:] = (rs.standard_normal(pool.k[0].shape) * KV_STD).astype(np.float32)
-    pool.v[0][:] = (rs.standard_normal(pool.v[0].shape) * KV_STD).astype(np.float32)
-    q = rs.standard_normal((N_SEQ, HQ, D)).astype(np.float32)
-    kn = (rs.standard_normal((N_SEQ, HKV, D)) * KV_STD).astype(np.float32)
-    vn = (rs.standard_normal((N_SEQ, HKV, D)) * KV_STD).astype(np.float32)
+    cs = CpuDecodeStep(args.seed, steps + warmup)
     times = []
     for s in range(warmup + steps):
-        m = build_meta(tables, ctx + s, [1] * N_SEQ, P)
-        t0 = time.perf_counter()
-        pool.append_kv(0, kn, vn, m.slot_mapping.numpy())
-        attend_reference(q, pool.k[0], pool.v[0], SCALE, m)
-        dt = time.perf_counter() - t0
+        dt = cs.step(cs.meta(s))
         if s >= warmup:
             times.append(dt)
-    per_layer = sum(times) / len(times)
-    step_s = per_layer * L  # one sampled layer per step, scaled to the 16-layer step
+    step_s = sum(times) / len(times)
     value = N_SEQ / step_s
     cores = cpu_threads()
-    sample = (f"each step: 1 of the 16 layers (append_kv + attend) over the full 256-sequence batch, "
-              f"float32 numpy port of PagedTorchBackend on {cores} BLAS threads; tok/s scaled to 16 layers")
+    sample = (f"every step: all 16 layers (append_kv + attend, each layer its own pool slab) over the full "
+              f"256-sequence batch, float32 numpy port of PagedTorchBackend on {cores} BLAS threads")
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": UNIT,
         "n_gpus": ws, "steps": steps, "warmup": warmup, "ms_per_step": round(step_s * 1e3, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic", "config": {"workload": WORKLOAD, "global_batch": N_SEQ * ws, "seq_len": 2048},
+        "data": "synthetic", "config": config_for(ws),
         "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+def config_for(ws: int) -> dict:
+    """The ``config`` of both arms' lines (the same keys and values)."""
+    return {"workload": WORKLOAD, "global_batch": N_SEQ * ws, "seq_len": 2048, "parallelism": f"replicas{ws}",
+            "l2": "inputs larger than L2 (~2.2 GB of KV read per step)"}
 
 
 # ------------------------------------------------------------------ B200 arm
@@ -434,14 +577,7 @@ def run_b200(args) -> None:
     alg_bytes = sum(alg) / len(alg)
     peak, peak_kind = measured_peaks()
     achieved = alg_bytes / (avg_launch_ms / 1e3) / 1e9
-    traffic = None
-    tfile = ROOT / "profiles" / "decode_traffic.json"
-    if tfile.exists():
-        try:
-            tj = json.loads(tfile.read_text())
-            traffic = round(float(tj["dram_bytes_per_alg_byte"]) * alg_bytes)
-        except Exception:
-            traffic = None
+    traffic, traffic_note = decode_traffic(alg_bytes)
 
     # ---- the same steps with append + attend fused into one launch per layer
     fused = None
@@ -520,26 +656,35 @@ def run_b200(args) -> None:
         dist.barrier()
 
     if rank == 0:
-        cpu = cpu_oracle_step_time(args.seed, args.cpu_budget) if args.cpu_budget > 0 else None
+        cpu = cpu_decode_rate(args.seed, args.cpu_budget) if args.cpu_budget > 0 else None
         cpu_line = None
         if cpu:
-            cpu_line = {"value": round(N_SEQ / (cpu["per_layer_s"] * L), 3), "unit": UNIT, "cores": cpu["cores"],
+            cpu_line = {"value": round(N_SEQ / cpu["step_s"], 3), "unit": UNIT, "cores": cpu["cores"],
                         "kind": "port",
-                        "sample": (f"{cpu['iters']} repetitions of one layer (append_kv + attend) over the full "
-                                   f"256-sequence batch (sum ctx {cpu['sum_ctx']}), float32 numpy restatement of "
-                                   "PagedTorchBackend; tok/s scaled to a 16-layer step")}
+                        "sample": (f"{cpu['steps']} whole 16-layer steps (append_kv + attend per layer, each layer "
+                                   f"its own pool slab) over the full 256-sequence batch (sum ctx "
+                                   f"{cpu['sum_ctx']}), float32 numpy restatement of PagedTorchBackend")}
+        if args.cpu_budget > 0 and "swap" in line_extra:
+            sw_cpu = cpu_swap_rate(args.seed, args.cpu_budget / 2)
+            line_extra["swap"]["cpu_baseline"] = {
+                "value": sw_cpu["d2h_gbs"], "unit": "GB/s", "h2d_gbs": sw_cpu["h2d_gbs"], "cores": sw_cpu["cores"],
+                "kind": "port", "sample": sw_cpu["sample"]}
+        if args.cpu_budget > 0 and "llama" in line_extra:
+            ll_cpu = cpu_llama_rate(args.seed, args.cpu_budget)
+            line_extra["llama"]["cpu_baseline"] = {
+                "value": ll_cpu["generated_tok_per_s"], "unit": "generated tok/s", "cores": ll_cpu["cores"],
+                "kind": "port", "ms_per_step": ll_cpu["ms_per_step"], "sample": ll_cpu["sample"]}
         line = {
             "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": ws, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "global_batch": N_SEQ * ws, "seq_len": 2048,
-                       "parallelism": f"replicas{ws}", "num_blocks": int(num_blocks),
-                       "pool_gb": round(bk.pool_bytes() / 1e9, 1), "distinct_steps": n_graphs,
-                       "l2": "inputs larger than L2 (~2.2 GB of KV read per step)"},
+            "config": config_for(ws),
+            "pool": {"num_blocks": int(num_blocks), "pool_gb": round(bk.pool_bytes() / 1e9, 1),
+                     "distinct_steps": n_graphs},
             "e2e": e2e,
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic,
-                         "peak_kind": peak_kind, "kernel": "decode_kernel",
+                         "peak_kind": peak_kind, "kernel": "decode_kernel", "traffic_source": traffic_note,
                          "alg_bytes_per_launch": int(alg_bytes), "avg_launch_us": round(avg_launch_ms * 1e3, 2),
                          "timing": ("CUDA events inside each timed step graph around its 16 back-to-back "
                                     "decode launches; mean launch = elapsed / 16"),
@@ -1120,10 +1265,11 @@ def run_llama(torch, bk, args, device, rank, feed="device", record=0) -> dict:
     every running sequence past its prompt and prefills at most 512 prompt
     tokens (the reference scheduler's max_prefill_tokens); a waiting request is
     admitted when a slot is free and prefill budget is left. Greedy sampling on
-    the GPU. ``feed="device"``: each sequence's last token stays on the GPU (a
-    token per block-table row) and the next step's input is assembled there
-    from it and the prompt tokens (host scheduling needs only lengths), while
-    the sampled tokens travel back asynchronously and are read one step later,
+    the GPU (``sample_greedy``, one launch). ``feed="device"``: each sequence's
+    last token stays on the GPU (a token per block-table row, written by the
+    sampling launch) and the next step's input is assembled there from it and
+    the prompt tokens (host scheduling needs only lengths), while the sampled
+    tokens travel back asynchronously (``TokenReadback``) and are read one step later,
     so the host never waits for the step it just issued; ``feed="sync"``: the
     step's tokens are read back before the next step is built. ``record``: the
     tokens sampled in the first ``record`` timed steps are returned (for the
@@ -1132,7 +1278,7 @@ def run_llama(torch, bk, args, device, rank, feed="device", record=0) -> dict:
     step's BatchMeta computed on the GPU). Wall clock per step: host scheduling
     and batch assembly, H2D of the step's rows / lengths / new blocks and
     tokens, the 16-layer forward, D2H of the tokens."""
-    from llm_serving_layer_b200 import DeviceBlockTables
+    from llm_serving_layer_b200 import DeviceBlockTables, TokenReadback, sample_greedy
     from llm_serving_layer_b200.llama import LlamaConfig, RandomLlama
 
     cfg = LlamaConfig()
@@ -1185,13 +1331,11 @@ def run_llama(torch, bk, args, device, rank, feed="device", record=0) -> dict:
     for r in running:
         init[r.row] = r.last
     last_dev.copy_(torch.from_numpy(init))
-    inflight = []  # (pinned tokens, event, per-entry sequences) of steps not read back yet
+    readback = TokenReadback(device)  # sampled tokens of the steps not read back yet
     recorded = []
 
     def read_back(upto):
-        while len(inflight) > upto:
-            host_tok, ev_done, who = inflight.pop(0)
-            ev_done.synchronize()
+        for who, host_tok in readback.collect(upto):
             if who is not None:
                 recorded.append(list(zip(who, host_tok.tolist())))
 
@@ -1227,21 +1371,19 @@ def run_llama(torch, bk, args, device, rank, feed="device", record=0) -> dict:
             # one packed transfer: the prompt tokens (0 where a decode row's token goes), the
             # decode rows' token positions and rows, and which entries sample a token into which row
             T = sum(q for _, q in batch)
-            dpos, drow, uj, urow = [], [], [], []
+            dpos, drow, srow = [], [], []
             o = 0
             for j, (r, q) in enumerate(batch):
                 if r.pos >= len(r.prompt):
                     dpos.append(o)
                     drow.append(r.row)
-                if r.pos >= len(r.prompt) or r.pos + q >= len(r.prompt):
-                    uj.append(j)
-                    urow.append(r.row)
+                srow.append(r.row if r.pos >= len(r.prompt) or r.pos + q >= len(r.prompt) else -1)
                 o += q
             packed = np.concatenate([np.concatenate([t if r.pos < len(r.prompt) else [0]
                                                      for (r, _), t in zip(batch, qtok)]).astype(np.int64),
-                                     dpos, drow, uj, urow]).astype(np.int64)
+                                     dpos, drow, srow]).astype(np.int64)
             dev_in = torch.from_numpy(packed).pin_memory().to(device, non_blocking=True)
-            nd, nu = len(dpos), len(uj)
+            nd = len(dpos)
             toks = dev_in[:T].clone()
             toks.index_copy_(0, dev_in[T:T + nd], last_dev.index_select(0, dev_in[T + nd:T + 2 * nd]))
         else:
@@ -1251,21 +1393,20 @@ def run_llama(torch, bk, args, device, rank, feed="device", record=0) -> dict:
         logits = model.forward_varlen(toks, meta, bk)
         ev[1].record()
         fwd_events.append(ev)
-        sampled = logits.argmax(-1)
         # the entries' identities, the same in both feeds (same seeds, same schedule), while recording
         who = ([(r.row, r.n) for r, _ in batch]
-               if counting[0] and len(recorded) + len(inflight) < record else None)
+               if counting[0] and len(recorded) + len(readback) < record else None)
         if feed == "device":
-            last_dev.index_copy_(0, dev_in[T + 2 * nd + nu:], sampled.index_select(0, dev_in[T + 2 * nd:T + 2 * nd + nu]))
-            host_tok = torch.empty(sampled.shape, dtype=sampled.dtype).pin_memory()
-            host_tok.copy_(sampled, non_blocking=True)
-            ev_done = torch.cuda.Event()
-            ev_done.record()
-            inflight.append((host_tok, ev_done, who))
+            # argmax of every entry's logits, written into its row's token (entries still
+            # mid-prompt have row -1 and write nothing), one launch; the tokens travel to the
+            # host on a side stream and are read one step later
+            sampled = sample_greedy(logits, tokens=last_dev, rows=dev_in[T + 2 * nd:].to(torch.int32),
+                                    status=bk._status)
+            readback.submit(sampled, who)
             read_back(1)  # the previous step's tokens: streamed one step behind
             nxt = [None] * len(batch)
         else:
-            nxt = sampled.cpu().tolist()
+            nxt = sample_greedy(logits).cpu().tolist()
             if who is not None:
                 recorded.append(list(zip(who, nxt)))
         gen = prompt_tok = 0
