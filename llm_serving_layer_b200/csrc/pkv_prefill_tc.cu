@@ -2,9 +2,20 @@
 // 5th-generation tensor cores: tcgen05 MMAs with their accumulators in tensor
 // memory (TMEM), operands staged in shared memory by TMA.
 //
-// One CTA = one tile of query rows of one sequence for ONE KV head: 128 rows =
-// TPT = 128 / G tokens x the G query heads that share the KV head (row
-// r = head * TPT + token). Warp roles:
+// Work item = one tile of query rows of one sequence for ONE KV head: 128 rows =
+// TPT = 128 / G tokens x the G query heads that share the KV head. Two kernels
+// share the roles and the per-block arithmetic:
+//   prefill_tc_kernel             one CTA per item (launches of at most one
+//                                 wave: 2 CTAs per SM); row r = head * TPT +
+//                                 token; the softmax threads load the query rows.
+//   prefill_tc_persistent_kernel  at most 2 CTAs per SM, each walking its share
+//                                 of the items (larger launches): TMEM and
+//                                 barriers are set up once, the producer loads
+//                                 each item's query tile by TMA into a double
+//                                 buffer (row r = token * G + head) ahead of its
+//                                 K/V blocks, and O is double-buffered in TMEM so
+//                                 one item's epilogue overlaps the next item's MMAs.
+// Warp roles:
 //   warp 0      TMA producer: one 2 KiB box per page per K and V (that head's
 //               [16 tok][64] slice), 4 pages = one 64-key block per stage,
 //               4 stages; pages past the tile's last visible key read the
@@ -16,8 +27,9 @@
 //                                    TMEM, B = V MN-major from shared memory)
 //               S is double-buffered in TMEM (columns 0-63 / 64-127), P is
 //               written over the first 32 columns of its S buffer as packed
-//               16-bit pairs, O lives in columns 128-191. Completion is
-//               signalled with tcgen05.commit to mbarriers.
+//               16-bit pairs, O lives in columns 128-191 (and 192-255, the
+//               persistent kernel's second O buffer). Completion is signalled
+//               with tcgen05.commit to mbarriers.
 //   warps 2-5   softmax, one thread per row (warp w reads TMEM lanes
 //               32*(w%4) .. +31): tcgen05.ld of the row's 64 scores, scale,
 //               bottom-right causal mask key <= kv_len - q_len + j (which also
@@ -30,6 +42,8 @@
 // Semantics are PagedTorchBackend.attend's (serving/backends/paged_torch.py:
 // 400-485): GQA head h reads KV head h // G, pages in listed order, mask
 // triu(diag = kv_len - q_len + 1).
+#include <algorithm>
+#include <cstdlib>
 #include <mutex>
 #include <string>
 #include <type_traits>
@@ -538,8 +552,477 @@ __global__ void __launch_bounds__(TC_THREADS, 2) prefill_tc_kernel(const __grid_
 
 size_t tc_smem() { return 1024 + TC_QTILE + size_t(TC_NST) * TC_STAGE + 256; }
 
+// 3-D TMA load (the query tile: dims D, query head, token).
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
+                                           int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cta.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
+// One work item: a tile of TPT tokens of sequence s (from j0) for KV head h.
+struct TcItem {
+  int bad;  // metadata inconsistent: the item is skipped by every role (and flagged)
+  int h, s, j0, q0, ql, lpl, kv, npages, n_pg, nblk;
+  int64_t pa;
+};
+
+// Every role derives the same items in the same order from the plan's tile
+// list (sorted by pages read, longest first): item w = tile w / n_kv, KV head
+// w % n_kv. `l2`: read through L2 (before griddepcontrol.wait).
+template <int TPT>
+__device__ __forceinline__ TcItem tc_item(const TcArgs& a, int w, bool l2) {
+  auto ld = [&](const int32_t* p) -> int32_t { return l2 ? __ldcg(p) : *p; };
+  TcItem it;
+  const int tile_idx = w / a.n_kv;
+  it.h = w - tile_idx * a.n_kv;
+  const int2 tile = l2 ? __ldcg(a.tiles + tile_idx) : a.tiles[tile_idx];
+  it.s = tile.x;
+  it.j0 = tile.y;
+  bool bad = it.s < 0 || it.s >= a.n_seqs;
+  int q0 = 0, ql = 0, lpl = 0;
+  int64_t pa = 0, pb = 0;
+  if (!bad) {
+    q0 = ld(a.cu_q + it.s);
+    ql = ld(a.cu_q + it.s + 1) - q0;
+    pa = ld(a.kv_indptr + it.s);
+    pb = ld(a.kv_indptr + it.s + 1);
+    lpl = ld(a.last_page_len + it.s);
+  }
+  const int64_t npages64 = pb - pa;
+  const int64_t kv64 = (npages64 - 1) * TC_P + lpl;
+  bad = bad || npages64 < 1 || pa < 0 || pb > a.total_pages || lpl < 1 || lpl > TC_P || ql < 1 ||
+        it.j0 < 0 || it.j0 >= ql || kv64 < ql || kv64 >= 0x7fffffff || q0 < 0 || q0 + ql > a.n_tokens;
+  if (!bad && a.kv_lens && ld(a.kv_lens + it.s) != kv64) bad = true;
+  it.bad = bad;
+  it.q0 = q0;
+  it.ql = ql;
+  it.lpl = lpl;
+  it.pa = pa;
+  it.kv = bad ? 0 : int(kv64);
+  it.npages = bad ? 0 : int(npages64);
+  it.n_pg = bad ? 0 : tc_tile_pages(it.kv, ql, it.j0, TPT);
+  it.nblk = (it.n_pg + TC_PPB - 1) / TC_PPB;
+  return it;
+}
+
+// The CTA's r-th item: rounds of gridDim.x items, walked forward on even rounds
+// and backward on odd ones, so that over the longest-first list every CTA's
+// total stays close to the others'.
+__device__ __forceinline__ int tc_item_index(int r) {
+  const int c = int(blockIdx.x), n = int(gridDim.x);
+  return r * n + ((r & 1) ? n - 1 - c : c);
+}
+
 template <typename T, int G>
-int launch_tc_t(const pkv_pool& p, const CUtensorMap& tm, const TcArgs& a, int grid, cudaStream_t s) {
+__global__ void __launch_bounds__(TC_THREADS, 2) prefill_tc_persistent_kernel(
+    const __grid_constant__ CUtensorMap tmap, const __grid_constant__ CUtensorMap qmap,
+                                                                   const TcArgs a) {
+  constexpr int TPT = TC_ROWS / G;  // tokens per tile
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char* qbuf = smem;                      // 2 x [128 rows][128 B], 128B swizzle
+  unsigned char* stages = smem + 2 * TC_QTILE;     // TC_NST x {K [64][128 B], V [64][128 B]}
+  uint64_t* full = reinterpret_cast<uint64_t*>(stages + size_t(TC_NST) * TC_STAGE);
+  uint64_t* empty = full + TC_NST;                 // P.V of the stage's block completed
+  uint64_t* s_full = empty + TC_NST;               // [2] S block in TMEM
+  uint64_t* p_full = s_full + 2;                   // [2] P in TMEM (and O rescaled), 128 arrivals
+  uint64_t* o_done = p_full + 2;                   // [2] P.V of global block g done: o_done[g & 1]
+  uint64_t* q_full = o_done + 2;                   // [2] query tile landed (TMA)
+  uint64_t* q_empty = q_full + 2;                  // [2] the item's S MMAs read their query tile
+  uint64_t* o_free = q_empty + 2;                  // [2] epilogue read O buffer, 128 arrivals
+  uint64_t* pg_bar = o_free + 2;                   // [2] page-id checks of the item gathered, 128 arrivals
+  uint64_t* drain = pg_bar + 2;                    // every MMA of the CTA completed
+  __shared__ uint32_t s_tmem;
+  __shared__ int s_pg_bad[2];
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_trigger();
+  // The plan kernel (tile list) completed before this kernel could start and
+  // fenced its stores: the item count may be read before griddepcontrol.wait.
+  const int n_items = __ldcg(a.n_tiles) * a.n_kv;
+  if (int(blockIdx.x) >= n_items) return;  // no item for this CTA (uniform over the CTA)
+
+  if (threadIdx.x == 0) {
+    prefetch_tmap(&tmap);
+    prefetch_tmap(&qmap);
+    for (int i = 0; i < TC_NST; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 128);
+      mbar_init(&o_done[i], 1);
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
+      mbar_init(&o_free[i], 128);
+      mbar_init(&pg_bar[i], 128);
+      s_pg_bad[i] = 0;
+    }
+    mbar_init(drain, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane < 2 * TC_PPB) {
+    // warm L2 with this head's slices of the first item's first two key blocks:
+    // a hint (no shared memory written), so it may run before the wait
+    const TcItem f = tc_item<TPT>(a, int(blockIdx.x), true);
+    if (!f.bad && lane < f.n_pg) {
+      const int id = __ldcg(a.kv_indices + f.pa + lane);
+      if (id >= 0 && id < a.num_blocks) {
+        tma_prefetch_l2_4d(&tmap, 0, id * TC_P, f.h, 2 * a.layer);
+        tma_prefetch_l2_4d(&tmap, 0, id * TC_P, f.h, 2 * a.layer + 1);
+      }
+    }
+  }
+  // ---- tensor memory: 256 columns S0 | S1 | O0 | O1, freed on every path below
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
+                 "r"(TC_TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = s_tmem;
+  pdl_wait();  // q and this layer's appended K/V rows are written by earlier kernels
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      const int kvc = 2 * a.layer;
+      uint32_t g = 0;  // global key-block counter of this CTA
+      int it = 0;      // good items started
+      bool dead = false;
+      for (int r = 0; !dead; ++r) {
+        const int w = tc_item_index(r);
+        if (w >= n_items) break;
+        const TcItem I = tc_item<TPT>(a, w, false);
+        if (I.bad) continue;
+        const int qb = it & 1;
+        if (it >= 2 && !mbar_wait_bounded_sleepy(&q_empty[qb], ((it - 2) >> 1) & 1, a.st, 64)) {
+          dead = true;
+          break;
+        }
+        mbar_arrive_expect_tx(&q_full[qb], TC_QTILE);
+        tma_load_3d(qbuf + qb * TC_QTILE, &qmap, &q_full[qb], 0, I.h * G, I.q0 + I.j0);
+        ++it;
+        for (int j = 0; j < I.nblk; ++j, ++g) {
+          const int st = int(g % TC_NST);
+          if (g >= TC_NST && !mbar_wait_bounded_sleepy(&empty[st], ((g / TC_NST) - 1) & 1, a.st, 64)) {
+            dead = true;
+            break;
+          }
+          unsigned char* kd = stages + size_t(st) * TC_STAGE;
+          mbar_arrive_expect_tx(&full[st], TC_STAGE);
+#pragma unroll
+          for (int u = 0; u < TC_PPB; ++u) {
+            const int pg = j * TC_PPB + u;
+            // a page past the tile's visible keys reads the zero fill of a negative coordinate
+            const int row = pg < I.n_pg ? a.kv_indices[I.pa + pg] * TC_P : -TC_P;
+            tma_load_4d(kd + u * TC_PAGE, &tmap, &full[st], 0, row, I.h, kvc);
+            tma_load_4d(kd + TC_KTILE + u * TC_PAGE, &tmap, &full[st], 0, row, I.h, kvc + 1);
+          }
+        }
+      }
+      if (dead) {
+        // let this CTA's own copies land before its shared memory can be released
+        for (uint32_t i = g > TC_NST ? g - TC_NST : 0; i < g; ++i)
+          mbar_wait_bounded(&full[i % TC_NST], (i / TC_NST) & 1, nullptr);
+        for (int i = it > 2 ? it - 2 : 0; i < it; ++i) mbar_wait_bounded(&q_full[i & 1], (i >> 1) & 1, nullptr);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    constexpr int fmt = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
+    constexpr uint32_t idS = idesc_f16(fmt, 0, TC_KB);
+    constexpr uint32_t idPV = idesc_f16(fmt, 1, TC_D);
+    uint32_t g = 0;
+    int it = 0;
+    bool dead = false;
+    for (int r = 0; !dead; ++r) {
+      const int w = tc_item_index(r);
+      if (w >= n_items) break;
+      const TcItem I = tc_item<TPT>(a, w, false);
+      if (I.bad) continue;
+      const int qb = it & 1;
+      const uint32_t tO = tbase + 128 + qb * TC_D;
+      if (!mbar_wait_bounded(&q_full[qb], (it >> 1) & 1, a.st)) dead = true;
+      dead = __any_sync(0xffffffffu, dead);
+      if (dead) break;
+      const uint32_t q_addr = smem_u32(qbuf + qb * TC_QTILE);
+      const int lp_blk = (I.npages - 1) / TC_PPB;  // block holding the sequence's last page
+      for (int j = 0; j <= I.nblk; ++j) {
+        if (j < I.nblk) {
+          const uint32_t gj = g + j;
+          const int st = int(gj % TC_NST);
+          if (!mbar_wait_bounded(&full[st], (gj / TC_NST) & 1, a.st)) dead = true;
+          dead = __any_sync(0xffffffffu, dead);
+          if (dead) break;
+          if (j == lp_blk && I.lpl < TC_P && I.npages - 1 < I.n_pg) {
+            // rows lpl..15 of the last page's V slice were never written: zero them
+            uint4* vt = reinterpret_cast<uint4*>(stages + size_t(st) * TC_STAGE + TC_KTILE +
+                                                 (I.npages - 1 - j * TC_PPB) * TC_PAGE);
+            for (int rr = I.lpl * 8 + lane; rr < TC_P * 8; rr += 32) vt[rr] = make_uint4(0u, 0u, 0u, 0u);
+            fence_proxy_async_smem();
+            __syncwarp();
+          }
+          if (lane == 0) {
+            tc_fence_after();
+            const uint32_t kaddr = smem_u32(stages + size_t(st) * TC_STAGE);
+            const uint32_t dS = tbase + (gj & 1) * TC_KB;
+#pragma unroll
+            for (int k = 0; k < TC_D / 16; ++k)
+              umma_ss(dS, sw128_desc(q_addr + 32 * k), sw128_desc(kaddr + 32 * k), idS, k > 0);
+            umma_commit(&s_full[gj & 1]);
+            if (j == I.nblk - 1) umma_commit(&q_empty[qb]);  // the item's last read of its query tile
+          }
+          __syncwarp();
+        }
+        if (j >= 1) {
+          const uint32_t gp = g + j - 1;
+          const int stp = int(gp % TC_NST);
+          if (!mbar_wait_bounded(&p_full[gp & 1], (gp >> 1) & 1, a.st)) dead = true;
+          // the item's first P.V overwrites this O buffer: the epilogue two items back read it
+          if (!dead && j == 1 && it >= 2 && !mbar_wait_bounded(&o_free[qb], ((it - 2) >> 1) & 1, a.st))
+            dead = true;
+          dead = __any_sync(0xffffffffu, dead);
+          if (dead) break;
+          if (lane == 0) {
+            tc_fence_after();
+            const uint32_t vaddr = smem_u32(stages + size_t(stp) * TC_STAGE + TC_KTILE);
+            const uint32_t aP = tbase + (gp & 1) * TC_KB;
+#pragma unroll
+            for (int k = 0; k < TC_KB / 16; ++k)
+              umma_ts(tO, aP + 8 * k, sw128_desc(vaddr + 16 * 128 * k), idPV, (j > 1 || k > 0) ? 1u : 0u);
+            umma_commit(&o_done[gp & 1]);
+            umma_commit(&empty[stp]);
+          }
+          __syncwarp();
+        }
+      }
+      g += I.nblk;
+      ++it;
+    }
+    // every MMA issued above has completed before TMEM is freed
+    if (lane == 0) {
+      umma_commit(drain);
+      mbar_wait_bounded(drain, 0, a.st);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ softmax warps
+    const int q4 = warp & 3;    // TMEM lane quarter this warp may access
+    const int r = q4 * 32 + lane;  // this thread's row: token r / G, query head r % G of the item's group
+    const uint32_t lane_off = uint32_t(q4 * 32) << 16;
+    const float sl2 = a.scale_log2;
+    T* out = static_cast<T*>(a.out);
+    uint32_t g = 0;
+    int it = 0;
+    bool dead = false;
+    for (int rr = 0; !dead; ++rr) {
+      const int w = tc_item_index(rr);
+      if (w >= n_items) break;
+      const TcItem I = tc_item<TPT>(a, w, false);
+      if (I.bad) {
+        if (r == 0) flag(a.st, PKV_DEV_META_BAD);
+        continue;
+      }
+      const int qb = it & 1;
+      const uint32_t tO = tbase + 128 + qb * TC_D;
+      // page ids of the item, checked while its blocks run (gathered at the epilogue)
+      bool pg_bad = false;
+      for (int p = r; p < I.n_pg; p += 128) {
+        const int id = a.kv_indices[I.pa + p];
+        pg_bad |= id < 0 || id >= a.num_blocks;
+      }
+      const int jq = I.j0 + r / G;
+      const bool valid = jq < I.ql;
+      const int lim = valid ? I.kv - I.ql + jq : -1;  // last visible key of this row
+      float m = -INFINITY, l = 0.f;
+      // Waits on o_done[x] happen in phase order on each barrier: block gj waits
+      // for P.V of block gj - 2 (its P buffer is about to be overwritten) and,
+      // only when it rescales O, for P.V of block gj - 1; the epilogue for the
+      // item's last block — so a try_wait on a parity never meets a barrier two
+      // phases ahead.
+      for (int j = 0; j < I.nblk; ++j) {
+        const uint32_t gj = g + j;
+        const int b = gj & 1;
+        if (!mbar_wait_bounded(&s_full[b], (gj >> 1) & 1, a.st)) dead = true;
+        if (j >= 2 && !dead && !mbar_wait_bounded(&o_done[b], ((gj - 2) >> 1) & 1, a.st)) dead = true;
+        dead = __any_sync(0xffffffffu, dead);
+        if (dead) break;
+        tc_fence_after();
+        uint32_t sr[64];
+        tmem_ld64(tbase + lane_off + b * TC_KB, sr);
+        const int kb0 = j * TC_KB;
+        if (sl2 <= 0.f) {  // a non-positive scale: scale first so the masked -inf stays the minimum
+#pragma unroll
+          for (int i = 0; i < 64; ++i) sr[i] = __float_as_uint(__uint_as_float(sr[i]) * sl2);
+        }
+        if (kb0 + TC_KB - 1 > lim) {  // the block reaches past this row's last visible key
+#pragma unroll
+          for (int i = 0; i < 64; ++i)
+            if (kb0 + i > lim) sr[i] = __float_as_uint(-INFINITY);
+        }
+        float mx;
+        {
+          float t[8];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) t[u] = __uint_as_float(sr[u]);
+#pragma unroll
+          for (int i = 8; i < 64; i += 2)
+            t[(i >> 1) & 7] = max3f(t[(i >> 1) & 7], __uint_as_float(sr[i]), __uint_as_float(sr[i + 1]));
+          mx = max3f(max3f(t[0], t[1], t[2]), max3f(t[3], t[4], t[5]), fmaxf(t[6], t[7]));
+        }
+        const float sc = sl2 > 0.f ? sl2 : 1.f;  // the scale still to apply (log2 units)
+        mx = mx * sc;                            // -inf stays -inf (sc > 0)
+        const float mn = fmaxf(m, mx);
+        float m_new = m;
+        if (mn != -INFINITY && (m == -INFINITY || mn > m + TC_RESCALE)) m_new = mn;
+        const bool resc = (m_new != m) && (m != -INFINITY);  // earlier blocks already added to O
+        const float alpha = resc ? ex2(m - m_new) : 1.f;
+        l *= alpha;
+        m = m_new;
+        if (__any_sync(0xffffffffu, resc)) {
+          // O holds P.V up to block gj - 1 (j >= 1 here): let that finish before reading it
+          if (!mbar_wait_bounded(&o_done[(gj - 1) & 1], ((gj - 1) >> 1) & 1, a.st)) dead = true;
+          dead = __any_sync(0xffffffffu, dead);
+          if (dead) break;
+          tc_fence_after();
+#pragma unroll
+          for (int hf = 0; hf < 2; ++hf) {
+            uint32_t o[32];
+            tmem_ld32(tO + lane_off + hf * 32, o);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            tmem_st32(tO + lane_off + hf * 32, o);
+          }
+        }
+        const float mu = m == -INFINITY ? 0.f : m;
+        const unsigned long long sc2 = f32x2(sc, sc), nmu2 = f32x2(-mu, -mu);
+        unsigned long long lt2[4] = {0ull, 0ull, 0ull, 0ull};  // pairs of running sums (0.f bits)
+        uint32_t pk[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          float x0, x1;
+          f32x2_split(fma_f32x2(f32x2(__uint_as_float(sr[2 * i]), __uint_as_float(sr[2 * i + 1])), sc2, nmu2), x0,
+                      x1);
+          const float p0 = ex2(x0), p1 = ex2(x1);
+          lt2[i & 3] = add_f32x2(lt2[i & 3], f32x2(p0, p1));
+          pk[i] = MmaOp<T>::pack(p0, p1);
+        }
+        float lt[8];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) f32x2_split(lt2[u], lt[2 * u], lt[2 * u + 1]);
+        const float ls = ((lt[0] + lt[1]) + (lt[2] + lt[3])) + ((lt[4] + lt[5]) + (lt[6] + lt[7]));
+        l += ls;
+        tmem_st32(tbase + lane_off + b * TC_KB, pk);
+        tc_fence_before();
+        mbar_arrive(&p_full[b]);
+      }
+      if (dead) break;
+      // ---- epilogue: O / l of the item -> global memory, while the MMA warp
+      // goes on with the next item into the other O buffer
+      const uint32_t gl = g + I.nblk - 1;
+      if (!mbar_wait_bounded(&o_done[gl & 1], (gl >> 1) & 1, a.st)) dead = true;
+      dead = __any_sync(0xffffffffu, dead);
+      if (dead) break;
+      tc_fence_after();
+      uint32_t o[2][32];
+      tmem_ld32(tO + lane_off, o[0]);
+      tmem_ld32(tO + lane_off + 32, o[1]);
+      tc_fence_before();
+      mbar_arrive(&o_free[qb]);
+      if (pg_bad) s_pg_bad[qb] = it + 1;
+      mbar_arrive(&pg_bar[qb]);
+      if (!mbar_wait_bounded(&pg_bar[qb], (it >> 1) & 1, a.st)) dead = true;
+      dead = __any_sync(0xffffffffu, dead);
+      if (dead) break;
+      const bool zero = s_pg_bad[qb] == it + 1;  // a page id outside the pool: the item's rows are zeros
+      if (zero && r == 0) flag(a.st, PKV_DEV_SLOT_OOB);
+      if (valid) {
+        T* orow = out + ((int64_t(I.q0) + jq) * a.n_heads + I.h * G + r % G) * TC_D;
+        const float inv = (l > 0.f && !zero) ? 1.f / l : 0.f;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const int e = c * 8;
+          uint4 v;
+          v.x = MmaOp<T>::pack(__uint_as_float(o[e >> 5][e & 31]) * inv, __uint_as_float(o[e >> 5][(e & 31) + 1]) * inv);
+          v.y = MmaOp<T>::pack(__uint_as_float(o[e >> 5][(e & 31) + 2]) * inv, __uint_as_float(o[e >> 5][(e & 31) + 3]) * inv);
+          v.z = MmaOp<T>::pack(__uint_as_float(o[e >> 5][(e & 31) + 4]) * inv, __uint_as_float(o[e >> 5][(e & 31) + 5]) * inv);
+          v.w = MmaOp<T>::pack(__uint_as_float(o[e >> 5][(e & 31) + 6]) * inv, __uint_as_float(o[e >> 5][(e & 31) + 7]) * inv);
+          if (zero) v = make_uint4(0u, 0u, 0u, 0u);
+          reinterpret_cast<uint4*>(orow)[c] = v;
+        }
+      }
+      g += I.nblk;
+      ++it;
+    }
+  }
+
+  // ---- free tensor memory once every role is done with it
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tbase), "r"(TC_TMEM_COLS)
+                 : "memory");
+  }
+}
+
+size_t tcp_smem() { return 1024 + 2 * size_t(TC_QTILE) + size_t(TC_NST) * TC_STAGE + 256; }
+
+// Which launches the persistent kernel takes: PKV_PREFILL_PERSISTENT unset or 1
+// = launches of more than one wave of CTAs, 0 = none (one CTA per tile for every
+// launch), 2 = every launch (for tests of the persistent kernel on small batches).
+int prefill_persistent_mode() {
+  static const int mode = [] {
+    const char* e = getenv("PKV_PREFILL_PERSISTENT");
+    if (e && e[0] == '0') return 0;
+    if (e && e[0] == '2') return 2;
+    return 1;
+  }();
+  return mode;
+}
+
+// Tensor map of the step's query rows q [n_tokens][n_heads][64] as dims
+// (D, query head, token): one box = the G heads of one KV head for TPT tokens,
+// landing in shared memory as row = token * G + head, 128B-swizzled (the
+// layout the S MMA's A operand descriptor reads).
+int q_tmap(int32_t dtype, const void* q, int n_tokens, int n_heads, int groups, CUtensorMap* out) {
+  static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+  if (!encode) {
+    cudaDriverEntryPointQueryResult qr;
+    void* fn = nullptr;
+    PKV_CUDA_RET(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &qr));
+    if (qr != cudaDriverEntryPointSuccess || !fn)
+      return fail(PKV_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+    encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  }
+  const cuuint64_t dims[3] = {cuuint64_t(TC_D), cuuint64_t(n_heads), cuuint64_t(std::max(n_tokens, 1))};
+  const cuuint64_t strides[2] = {cuuint64_t(TC_D) * 2, cuuint64_t(n_heads) * TC_D * 2};
+  const cuuint32_t box[3] = {cuuint32_t(TC_D), cuuint32_t(groups), cuuint32_t(TC_ROWS / groups)};
+  const cuuint32_t estr[3] = {1u, 1u, 1u};
+  const CUtensorMapDataType dt =
+      dtype == PKV_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = encode(out, dt, 3, const_cast<void*>(q), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                      CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(PKV_ERR_CUDA, "cuTensorMapEncodeTiled (q) failed: " + std::to_string(int(r)));
+  return PKV_OK;
+}
+
+
+// Launches one of the two kernels: `qm` == nullptr -> one CTA per (tile, KV
+// head) (prefill_tc_kernel), otherwise the persistent kernel over `grid` CTAs.
+template <typename T, int G>
+int launch_tc_t(const pkv_pool& p, const CUtensorMap& tm, const CUtensorMap* qm, const TcArgs& a, int grid,
+                cudaStream_t s) {
   static std::mutex mu;
   static std::vector<char> ready;
   int dev = 0;
@@ -550,20 +1033,27 @@ int launch_tc_t(const pkv_pool& p, const CUtensorMap& tm, const TcArgs& a, int g
     if (!ready[dev]) {
       PKV_CUDA_RET(cudaFuncSetAttribute(prefill_tc_kernel<T, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         int(tc_smem())));
+      PKV_CUDA_RET(cudaFuncSetAttribute(prefill_tc_persistent_kernel<T, G>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, int(tcp_smem())));
       ready[dev] = 1;
     }
   }
-  PKV_CUDA_RET(launch_kernel(prefill_tc_kernel<T, G>, dim3(grid), dim3(TC_THREADS), tc_smem(), s, true, tm, a));
+  if (qm)
+    PKV_CUDA_RET(launch_kernel(prefill_tc_persistent_kernel<T, G>, dim3(grid), dim3(TC_THREADS), tcp_smem(), s,
+                               true, tm, *qm, a));
+  else
+    PKV_CUDA_RET(launch_kernel(prefill_tc_kernel<T, G>, dim3(grid), dim3(TC_THREADS), tc_smem(), s, true, tm, a));
   return PKV_OK;
 }
 
 template <typename T>
-int launch_tc_g(const pkv_pool& p, int groups, const CUtensorMap& tm, const TcArgs& a, int grid, cudaStream_t s) {
+int launch_tc_g(const pkv_pool& p, int groups, const CUtensorMap& tm, const CUtensorMap* qm, const TcArgs& a,
+                int grid, cudaStream_t s) {
   switch (groups) {
-    case 1: return launch_tc_t<T, 1>(p, tm, a, grid, s);
-    case 2: return launch_tc_t<T, 2>(p, tm, a, grid, s);
-    case 4: return launch_tc_t<T, 4>(p, tm, a, grid, s);
-    case 8: return launch_tc_t<T, 8>(p, tm, a, grid, s);
+    case 1: return launch_tc_t<T, 1>(p, tm, qm, a, grid, s);
+    case 2: return launch_tc_t<T, 2>(p, tm, qm, a, grid, s);
+    case 4: return launch_tc_t<T, 4>(p, tm, qm, a, grid, s);
+    case 8: return launch_tc_t<T, 8>(p, tm, qm, a, grid, s);
   }
   return fail(PKV_ERR_UNSUPPORTED, "tcgen05 prefill kernel: unsupported GQA group size");
 }
@@ -601,11 +1091,23 @@ int prefill_tc_attend(const pkv_pool& p, int layer, int n_heads, const void* q, 
   a.early_ctas = 2 * num_sms();  // two CTAs per SM (__launch_bounds__ and shared memory)
   const int qt = prefill_tc_tile_tokens(n_heads, p.n_kv_heads);
   const int64_t bound = std::min<int64_t>((int64_t(b.n_tokens) + qt - 1) / qt + b.n_seqs, tiles_cap);
-  const int64_t grid = std::max<int64_t>(1, bound) * p.n_kv_heads;
-  if (grid > 0x7fffffff) return fail(PKV_ERR_ARG, "prefill batch too large for one launch");
+  const int64_t items = std::max<int64_t>(1, bound) * p.n_kv_heads;
   const int groups = n_heads / p.n_kv_heads;
-  if (p.dtype == PKV_F16) return launch_tc_g<__half>(p, groups, tm, a, int(grid), s);
-  return launch_tc_g<__nv_bfloat16>(p, groups, tm, a, int(grid), s);
+  const int64_t slots = int64_t(2) * num_sms();  // resident CTAs (two per SM)
+  CUtensorMap qm;
+  const CUtensorMap* qmp = nullptr;
+  int64_t grid = items;
+  const int mode = prefill_persistent_mode();
+  if ((mode == 1 && items > slots) || mode == 2) {
+    // more tiles than one wave: persistent CTAs walk the tiles (each CTA's
+    // setup, query loads and epilogues overlap its other tiles' work)
+    if (int rc = q_tmap(p.dtype, q, b.n_tokens, n_heads, groups, &qm)) return rc;
+    qmp = &qm;
+    grid = std::min(items, slots);
+  }
+  if (grid > 0x7fffffff) return fail(PKV_ERR_ARG, "prefill batch too large for one launch");
+  if (p.dtype == PKV_F16) return launch_tc_g<__half>(p, groups, tm, qmp, a, int(grid), s);
+  return launch_tc_g<__nv_bfloat16>(p, groups, tm, qmp, a, int(grid), s);
 }
 
 }  // namespace pkv
