@@ -1474,6 +1474,115 @@ def run_llama(torch, bk, args, device, rank, feed="device", record=0) -> dict:
             "timing": "host wall clock around the steps (host scheduling, batch assembly, H2D, forward, D2H)"}
 
 
+def run_flashinfer(args) -> None:
+    """The reference's own GPU path on the same B200, as a comparison (not a
+    bench line): FlashInfer's BatchDecodeWithPagedKVCacheWrapper(use_tensor_cores
+    = False) and BatchPrefillWithPagedKVCacheWrapper (default backend), planned
+    once per step and run per layer on (k_pool[l], v_pool[l]) in "NHD" layout
+    exactly as the reference configures them
+    (serving/backends/flashinfer_backend.py:336-345, 602-676), against this
+    package's planned attention on the same pool, page tables and queries:
+    config 2's decode steps (16 layers, batch 256) and config 3's prefill steps
+    (16 layers). Kernel time on the device (CUDA events around each step's 16
+    back-to-back attention launches, after the step's plan); the outputs are
+    compared. One JSON line."""
+    import torch
+
+    import flashinfer as fi
+    from llm_serving_layer_b200 import B200PagedBackend
+    from llm_serving_layer_b200.meta import build_meta
+
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    free, total = torch.cuda.mem_get_info(device)
+    block_bytes = B200PagedBackend.estimate_pool_bytes(L, 1, P, HKV, D, torch.float16)
+    num_blocks = int(min(0.3 * total, free - (16 << 30)) // block_bytes)
+    bk = B200PagedBackend(L, num_blocks, P, HKV, HQ, D, device=device, dtype=torch.float16, validate="device")
+    rs = np.random.RandomState(args.seed)
+    n_steps = 12
+    ctx, tables, metas = build_workload(torch, bk, rs, n_steps, device)
+    g = torch.Generator(device=device).manual_seed(args.seed)
+    qs = [torch.randn((N_SEQ, HQ, D), generator=g, device=device).half() for _ in range(L)]
+    ws = [torch.zeros(128 << 20, dtype=torch.uint8, device=device) for _ in range(2)]
+    dec = fi.BatchDecodeWithPagedKVCacheWrapper(ws[0], "NHD", use_tensor_cores=False)
+    pre = fi.BatchPrefillWithPagedKVCacheWrapper(ws[1], "NHD")
+    kv = [(bk.k_pool[l], bk.v_pool[l]) for l in range(L)]
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def timed(fn):
+        e0.record()
+        outs = fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) * 1e3, outs
+
+    def fi_plan_decode(m):
+        dec.plan(m.kv_indptr, m.kv_indices, m.kv_last_page_len, HQ, HKV, D, P, pos_encoding_mode="NONE",
+                 sm_scale=SCALE, q_data_type=torch.float16, kv_data_type=torch.float16)
+
+    res = {"flashinfer_version": fi.__version__}
+    # ---- decode (config 2)
+    ours_us, fi_us, diff = [], [], 0.0
+    for rep in range(2):
+        for m in metas:
+            bk.invalidate_plan()
+            bk.plan(m)
+            torch.cuda.synchronize()
+            t, a = timed(lambda: [bk.attend(qs[l], l, SCALE, m) for l in range(L)])
+            fi_plan_decode(m)
+            torch.cuda.synchronize()
+            t2, b = timed(lambda: [dec.run(qs[l], kv[l]) for l in range(L)])
+            if rep:
+                ours_us.append(t / L)
+                fi_us.append(t2 / L)
+                diff = max(diff, max(float((x.float() - y.float()).abs().max()) for x, y in zip(a, b)))
+    res["decode"] = {"workload": "config 2 decode steps (256 sequences, lognormal ctx mean ~258), 16 layers",
+                     "ours_us_per_layer": round(float(np.mean(ours_us)), 2),
+                     "flashinfer_us_per_layer": round(float(np.mean(fi_us)), 2),
+                     "speedup": round(float(np.mean(fi_us)) / float(np.mean(ours_us)), 2),
+                     "max_abs_diff": round(diff, 5),
+                     "flashinfer_path": "BatchDecodeWithPagedKVCacheWrapper(use_tensor_cores=False), plan per step"}
+    # ---- chunked prefill (config 3)
+    work = prefill_workload(args.seed + 3)
+    perm = np.random.RandomState(args.seed + 5).permutation(bk.num_blocks)
+    remap = {}
+
+    def blk(b):
+        if b not in remap:
+            remap[b] = int(perm[len(remap)])
+        return remap[b]
+
+    ptables = {i: [blk(b) for b in t] for i, t in work["tables"].items()}
+    qb = [torch.randn((512, HQ, D), generator=g, device=device).half() for _ in range(L)]
+    ours_us, fi_us, diff, steps_used = [], [], 0.0, 0
+    for ids, st, en in work["steps"][:: max(1, len(work["steps"]) // 60)]:
+        tabs = [ptables[i][:(e + P - 1) // P] for i, e in zip(ids, en)]
+        m = build_meta(tabs, en, [e - s for s, e in zip(st, en)], P, device=device)
+        T = int(m.positions.shape[0])
+        bk.invalidate_plan()
+        bk.plan(m)
+        pre.plan(m.cu_query_lens, m.kv_indptr, m.kv_indices, m.kv_last_page_len, HQ, HKV, D, P, causal=True,
+                 pos_encoding_mode="NONE", sm_scale=SCALE, q_data_type=torch.float16, kv_data_type=torch.float16)
+        torch.cuda.synchronize()
+        for rep in range(2):
+            t, a = timed(lambda: [bk.attend(qb[l][:T], l, SCALE, m) for l in range(L)])
+            t2, b = timed(lambda: [pre.run(qb[l][:T], kv[l]) for l in range(L)])
+        ours_us.append(t / L)
+        fi_us.append(t2 / L)
+        diff = max(diff, max(float((x.float() - y.float()).abs().max()) for x, y in zip(a, b)))
+        steps_used += 1
+    res["prefill"] = {"workload": f"config 3 prefill steps ({steps_used} of {len(work['steps'])}, every "
+                                  f"{max(1, len(work['steps']) // 60)}th; <= 512 prompt tokens each), 16 layers",
+                      "ours_us_per_layer": round(float(np.mean(ours_us)), 2),
+                      "flashinfer_us_per_layer": round(float(np.mean(fi_us)), 2),
+                      "speedup": round(float(np.mean(fi_us)) / float(np.mean(ours_us)), 2),
+                      "max_abs_diff": round(diff, 5),
+                      "flashinfer_path": "BatchPrefillWithPagedKVCacheWrapper (default backend: fa2 on sm_100), "
+                                         "causal, plan per step"}
+    res["timing"] = "CUDA events around each step's 16 back-to-back attention launches, after the step's plan"
+    print(json.dumps(res), flush=True)
+
+
 def decode_sweep() -> None:
     """The decode kernel against batch size: for 64-2048 sequences with config
     2's context distribution (scattered pages of a pool sized for the largest
@@ -1610,6 +1719,8 @@ def main() -> None:
     ap.add_argument("--llama-steps", type=int, default=100)
     ap.add_argument("--kvops-probe", action="store_true",
                     help="run only the small append / copy-on-write / swap workload (for kernel profilers)")
+    ap.add_argument("--flashinfer", action="store_true",
+                    help="compare against FlashInfer (the reference's GPU backend) on config 2 and 3 inputs")
     ap.add_argument("--decode-sweep", action="store_true",
                     help="run only the decode kernel over batch sizes 64-2048 (one JSON line per size)")
     args = ap.parse_args()
@@ -1618,6 +1729,9 @@ def main() -> None:
         return
     if args.decode_sweep:
         decode_sweep()
+        return
+    if args.flashinfer:
+        run_flashinfer(args)
         return
     args.warmup = max(3, args.warmup)
     if args.impl == "reference":
