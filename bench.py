@@ -1583,6 +1583,126 @@ def run_flashinfer(args) -> None:
     print(json.dumps(res), flush=True)
 
 
+def radix_host(args) -> None:
+    """Host time per scheduler step of the block-manager and prefix-cache work
+    at 1024 running sequences (config 5's batch): this package's BlockAllocator
+    + RadixCache (llm_serving_layer_b200.radix) and, when a reference checkout is
+    named by LLM_SERVING_LAYER_REF, the reference's own classes on the same
+    operations. Pool of 60 000 16-token blocks; 64 prompt families; before
+    timing, published prefixes that no sequence holds fill the rest of the pool
+    (as after a long run), so every admission evicts. Each step: every running sequence grows by one token (a block
+    when it crosses a page), 6 retire (publish, free), 6 arrive (lookup,
+    reserve with eviction, attach, allocate the rest). Reported: median host
+    ms per step, with and without the allocator's invariant check after each
+    step (the reference's debug mode: a full check; here also the O(1)
+    incremental one). One JSON line; CPU only."""
+    import importlib
+    import os
+
+    def make(mod_alloc, mod_radix, seq_cls):
+        return mod_alloc.BlockAllocator, mod_radix.RadixCache, mod_radix.attach_prefix, seq_cls
+
+    class _Seq:
+        def __init__(self, alloc, seq_id=0):
+            self.alloc, self.seq_id, self.block_size = alloc, seq_id, alloc.block_size
+            self.block_ids, self.num_tokens, self.is_freed = [], 0, False
+
+        def blocks_needed_for(self, n):
+            return max(0, (self.num_tokens + n + self.block_size - 1) // self.block_size - len(self.block_ids))
+
+        def append(self, n):
+            need = self.blocks_needed_for(n)
+            if need:
+                self.block_ids.extend(self.alloc.allocate(need))
+            self.num_tokens += n
+
+        def free(self):
+            if not self.is_freed and self.block_ids:
+                self.alloc.free(self.block_ids)
+            self.block_ids, self.num_tokens, self.is_freed = [], 0, True
+
+    import llm_serving_layer_b200.radix as ours
+    impls = {"b200": make(ours, ours, _Seq)}
+    ref_root = os.environ.get("LLM_SERVING_LAYER_REF", "")
+    if ref_root and Path(ref_root, "serving", "cache", "radix.py").is_file():
+        import types
+        import llm_serving_layer_b200.meta as meta_mod
+        eng = types.ModuleType("engine")
+        eng.attention_backend = meta_mod
+        sys.modules.setdefault("engine", eng)
+        sys.modules.setdefault("engine.attention_backend", meta_mod)
+        sys.path.insert(0, ref_root)
+        impls["reference"] = make(importlib.import_module("serving.memory.allocator"),
+                                  importlib.import_module("serving.cache.radix"), _Seq)
+
+    def run(impl, check: bool, steps: int):
+        BA, RC, attach, Seq = impl
+        rs = np.random.RandomState(args.seed)
+        alloc = BA(num_blocks=60000, block_size=P, watermark_blocks=64)
+        cache = RC(alloc)
+        fams = [list(rs.randint(0, 32000, size=int(rs.randint(64, 512)))) for _ in range(64)]
+        running = []
+
+        def admit():
+            f = fams[rs.randint(len(fams))]
+            toks = f[: int(rs.randint(16, len(f) + 1))] + list(rs.randint(0, 32000, size=int(rs.randint(16, 200))))
+            seq = Seq(alloc)
+            res = cache.acquire(toks)
+            if res.block_ids:
+                attach(seq, res.block_ids, res.n_tokens)
+            cache.reserve(seq.blocks_needed_for(len(toks) - res.n_tokens), watermark=False)
+            seq.append(len(toks) - res.n_tokens)
+            running.append([seq, toks, int(rs.randint(16, 400))])
+
+        while len(running) < 1024:
+            admit()
+        # the cache fills the rest of the pool with published, unused prefixes (as after a
+        # long run), so every admission below has to evict
+        while alloc.num_free > 200:
+            f = fams[rs.randint(len(fams))]
+            toks = f[: int(rs.randint(16, len(f) + 1))] + list(rs.randint(0, 32000, size=int(rs.randint(16, 200))))
+            seq = Seq(alloc)
+            seq.append(min(len(toks), P * (alloc.num_free - 100)))
+            cache.insert(toks[: seq.num_tokens], seq.block_ids)
+            seq.free()
+        times = []
+        for st in range(steps):
+            t0 = time.perf_counter()
+            for r in running:  # one token each; a new block when a page fills
+                if r[0].blocks_needed_for(1):
+                    cache.reserve(1, watermark=False)
+                r[0].append(1)
+                r[1].append(7)
+                r[2] -= 1
+            for _ in range(6):  # retire: publish, then free
+                i = max(range(len(running)), key=lambda j: -running[j][2]) if st % 2 else rs.randint(len(running))
+                seq, toks, _ = running.pop(i)
+                cache.insert(toks[: seq.num_tokens], seq.block_ids)
+                seq.free()
+            for _ in range(6):
+                admit()
+            if check == "full":
+                alloc.check_invariants()
+            elif check == "incremental":
+                alloc.check_invariants(full=False)
+            times.append(time.perf_counter() - t0)
+        return {"ms_per_step_median": round(1e3 * statistics.median(times[2:]), 3),
+                "cached_blocks": cache.cached_blocks, "evictions": cache.stats.evictions,
+                "free_blocks": alloc.num_free}
+
+    out = {"workload": ("block manager + radix prefix cache host work per scheduler step at 1024 running "
+                        "sequences: 60000 16-token blocks (the rest of the pool held by cached prefixes), 64 prompt families, 6 arrivals and 6 retirements "
+                        "per step, every sequence +1 token"), "steps": args.radix_steps}
+    for name, impl in impls.items():
+        out[name] = {"no_check": run(impl, None, args.radix_steps),
+                     "full_check_every_step": run(impl, "full", args.radix_steps)}
+        if name == "b200":
+            out[name]["incremental_check_every_step"] = run(impl, "incremental", args.radix_steps)
+    if "reference" not in impls:
+        out["reference"] = "not run: set LLM_SERVING_LAYER_REF to a reference checkout to time its classes beside"
+    print(json.dumps(out), flush=True)
+
+
 def decode_sweep() -> None:
     """The decode kernel against batch size: for 64-2048 sequences with config
     2's context distribution (scattered pages of a pool sized for the largest
@@ -1719,6 +1839,9 @@ def main() -> None:
     ap.add_argument("--llama-steps", type=int, default=100)
     ap.add_argument("--kvops-probe", action="store_true",
                     help="run only the small append / copy-on-write / swap workload (for kernel profilers)")
+    ap.add_argument("--radix-host", action="store_true",
+                    help="CPU only: host time per step of the block allocator and radix cache at 1024 sequences")
+    ap.add_argument("--radix-steps", type=int, default=40)
     ap.add_argument("--flashinfer", action="store_true",
                     help="compare against FlashInfer (the reference's GPU backend) on config 2 and 3 inputs")
     ap.add_argument("--decode-sweep", action="store_true",
@@ -1732,6 +1855,9 @@ def main() -> None:
         return
     if args.flashinfer:
         run_flashinfer(args)
+        return
+    if args.radix_host:
+        radix_host(args)
         return
     args.warmup = max(3, args.warmup)
     if args.impl == "reference":

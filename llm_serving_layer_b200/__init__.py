@@ -13,6 +13,10 @@ Drop-ins behind the reference's own interfaces:
   and a vectorised host assembler;
 * ``DeviceBlockTables`` — block tables kept on the device and each step's
   ``BatchMeta`` assembled there, replacing the engine's ``build_batch_meta``;
+* ``BlockAllocator`` / ``RadixCache`` / ``attach_prefix`` (``radix``) — the
+  block manager and prefix cache the scheduler drives, with eviction in
+  O(log nodes) and an O(1) invariant check, replacing
+  ``serving.memory.allocator`` / ``serving.cache.radix``;
 * ``sample_greedy`` / ``TokenReadback`` — greedy sampling on the device into a
   device token table, with the host reading the tokens a step later,
   replacing the scheduler's ``torch.argmax(logits).tolist()``.
@@ -23,6 +27,7 @@ All compute runs in ``_lib/libpkv.so`` (hand-written CUDA, C ABI in
 
 from .backend import B200PagedBackend
 from .meta import AttentionBackend, BatchMeta, build_meta
+from .radix import BlockAllocator, RadixCache, attach_prefix
 from .sampling import TokenReadback, sample_greedy
 from .swap import B200SwapSpace, SwapHandle, SwapSpaceFull
 from .tables import DeviceBlockTables
@@ -36,6 +41,9 @@ __all__ = [
     "AttentionBackend",
     "build_meta",
     "DeviceBlockTables",
+    "BlockAllocator",
+    "RadixCache",
+    "attach_prefix",
     "sample_greedy",
     "TokenReadback",
 ]
