@@ -457,7 +457,20 @@ def run_b200(args) -> None:
     from llm_serving_layer_b200.meta import build_meta
 
     ws, rank, local = dist_env()
+    host_cores = None
     if ws > 1:
+        # each replica's host work (batch assembly, launches, copies) on its own share of the cores
+        try:
+            cores = sorted(os.sched_getaffinity(0))
+            lws = int(os.environ.get("LOCAL_WORLD_SIZE", ws))
+            per = max(1, len(cores) // max(1, lws))
+            mine = cores[local * per:(local + 1) * per] or cores
+            os.sched_setaffinity(0, mine)
+            torch.set_num_threads(len(mine))
+            host_cores = len(mine)
+        except (AttributeError, OSError):
+            host_cores = None
+        args.cpu_budget = 0  # the CPU baselines are timed on rank 0 of a one-GPU run only
         dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
     torch.cuda.set_device(local)
@@ -681,6 +694,7 @@ def run_b200(args) -> None:
             "config": config_for(ws),
             "pool": {"num_blocks": int(num_blocks), "pool_gb": round(bk.pool_bytes() / 1e9, 1),
                      "distinct_steps": n_graphs},
+            "host_cores_per_rank": host_cores,
             "e2e": e2e,
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic,
