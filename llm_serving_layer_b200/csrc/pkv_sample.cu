@@ -17,9 +17,11 @@
 //
 // HBM-bound (one pass over the logits: 2 or 4 B per element). A CTA of 512
 // threads streams its share of a row with 16-byte loads, four in flight per
-// thread. Small batches (fewer rows than two CTAs per SM) split each row over a
-// thread-block cluster of 2-8 CTAs; the cluster combines its partial maxima
-// through distributed shared memory, so no global scratch and no atomics.
+// thread; per 16-byte vector only its maximum is compared with the thread's
+// best (the vector is searched for the index only when that beats it). Small
+// batches (fewer rows than two CTAs per SM) split each row over a thread-block
+// cluster of 2-8 CTAs; the cluster combines its partial maxima through
+// distributed shared memory, so no global scratch and no atomics.
 #include <cooperative_groups.h>
 
 #include <algorithm>
@@ -43,6 +45,8 @@ __device__ __forceinline__ uint32_t order_key(float v) {
 
 template <typename T>
 struct Vec;
+// Vec<T>::vmax: the largest of a vector's elements, a NaN if it holds one (the
+// order_key order up to the sign of zero, which order_key folds).
 template <>
 struct Vec<float> {
   static constexpr int N = 4;
@@ -51,6 +55,12 @@ struct Vec<float> {
     f[1] = __uint_as_float(u.y);
     f[2] = __uint_as_float(u.z);
     f[3] = __uint_as_float(u.w);
+  }
+  __device__ __forceinline__ static float vmax(const uint4& u) {
+    const float a = __uint_as_float(u.x), b = __uint_as_float(u.y), c = __uint_as_float(u.z),
+                d = __uint_as_float(u.w);
+    const float m = fmaxf(fmaxf(a, b), fmaxf(c, d));  // fmaxf drops NaNs: put one back
+    return (a != a || b != b || c != c || d != d) ? __uint_as_float(0x7fffffffu) : m;
   }
 };
 template <>
@@ -65,6 +75,13 @@ struct Vec<__half> {
       f[2 * i + 1] = p.y;
     }
   }
+  __device__ __forceinline__ static float vmax(const uint4& u) {
+    const __half2 m = __hmax2_nan(__hmax2_nan(*reinterpret_cast<const __half2*>(&u.x),
+                                              *reinterpret_cast<const __half2*>(&u.y)),
+                                  __hmax2_nan(*reinterpret_cast<const __half2*>(&u.z),
+                                              *reinterpret_cast<const __half2*>(&u.w)));
+    return __half2float(__hmax_nan(__low2half(m), __high2half(m)));
+  }
 };
 template <>
 struct Vec<__nv_bfloat16> {
@@ -78,10 +95,36 @@ struct Vec<__nv_bfloat16> {
       f[2 * i + 1] = p.y;
     }
   }
+  __device__ __forceinline__ static float vmax(const uint4& u) {
+    const __nv_bfloat162 m = __hmax2_nan(__hmax2_nan(*reinterpret_cast<const __nv_bfloat162*>(&u.x),
+                                                     *reinterpret_cast<const __nv_bfloat162*>(&u.y)),
+                                         __hmax2_nan(*reinterpret_cast<const __nv_bfloat162*>(&u.z),
+                                                     *reinterpret_cast<const __nv_bfloat162*>(&u.w)));
+    return __bfloat162float(__hmax_nan(__low2bfloat16(m), __high2bfloat16(m)));
+  }
 };
 
 __device__ __forceinline__ uint64_t pack_best(uint32_t key, uint32_t idx) {
   return (uint64_t(key) << 32) | uint64_t(~idx);
+}
+
+// A vector of elements [base, base + N): its maximum's key is compared with
+// the thread's best; only a vector that beats it is searched for the first
+// element holding that key (rare once a row's large values have been seen).
+template <typename T>
+__device__ __forceinline__ void take_vec(const uint4& u, uint32_t base, uint32_t& best_key, uint32_t& best_idx) {
+  constexpr int N = Vec<T>::N;
+  const uint32_t vk = order_key(Vec<T>::vmax(u));
+  if (vk > best_key) {
+    float f[N];
+    Vec<T>::unpack(u, f);
+    int first = N - 1;
+#pragma unroll
+    for (int e = N - 1; e >= 0; --e)
+      if (order_key(f[e]) == vk) first = e;
+    best_key = vk;
+    best_idx = base + first;
+  }
 }
 
 // One CTA's share of a row: [lo, hi) element indices. Threads visit their
@@ -102,33 +145,10 @@ __device__ __forceinline__ uint64_t scan_share(const T* __restrict__ row, int64_
 #pragma unroll
       for (int j = 0; j < SG_UNROLL; ++j) u[j] = __ldcs(v + k + int64_t(j) * SG_THREADS);
 #pragma unroll
-      for (int j = 0; j < SG_UNROLL; ++j) {
-        float f[N];
-        Vec<T>::unpack(u[j], f);
-        const uint32_t base = uint32_t(lo + (k + int64_t(j) * SG_THREADS) * N);
-#pragma unroll
-        for (int e = 0; e < N; ++e) {
-          const uint32_t key = order_key(f[e]);
-          if (key > best_key) {
-            best_key = key;
-            best_idx = base + e;
-          }
-        }
-      }
+      for (int j = 0; j < SG_UNROLL; ++j)
+        take_vec<T>(u[j], uint32_t(lo + (k + int64_t(j) * SG_THREADS) * N), best_key, best_idx);
     }
-    for (; k < nvec; k += SG_THREADS) {
-      float f[N];
-      Vec<T>::unpack(__ldcs(v + k), f);
-      const uint32_t base = uint32_t(lo + k * N);
-#pragma unroll
-      for (int e = 0; e < N; ++e) {
-        const uint32_t key = order_key(f[e]);
-        if (key > best_key) {
-          best_key = key;
-          best_idx = base + e;
-        }
-      }
-    }
+    for (; k < nvec; k += SG_THREADS) take_vec<T>(__ldcs(v + k), uint32_t(lo + k * N), best_key, best_idx);
     i = lo + nvec * N;
   }
   for (int64_t e = i + threadIdx.x; e < hi; e += SG_THREADS) {
