@@ -53,7 +53,7 @@ struct WsLayout {
   size_t counters = 0;   // int32[n_seqs]: split pieces counted in, per sequence
   size_t partial_o = 0;   // float[2 * grid][n_heads][D]
   size_t partial_ml = 0;  // float2[2 * grid][n_heads]
-  size_t n_tiles = 0;     // int32: prefill tiles planned (prefill layout only)
+  size_t n_tiles = 0;     // int32[3]: prefill tiles planned, the lean prefill kernel's claim and exit counters (prefill layout only)
   size_t p_dec = 0;       // int64: decode-row pages listed in a mixed batch (prefill layout only)
   size_t rows = 0;        // int32[n_seqs]: their q / out rows (prefill layout only)
   size_t tiles = 0;       // int2[tiles_cap] {seq, first token} (prefill layout only)
@@ -78,7 +78,7 @@ WsLayout ws_layout(int n_heads, int n_seqs, int64_t total_pages, int max_grid, i
   off = align256(off + sizeof(float2) * size_t(2) * max_grid * n_heads);
   if (tiles_cap > 0) {
     w.n_tiles = off;
-    off = align256(off + sizeof(int32_t));
+    off = align256(off + 3 * sizeof(int32_t));
     w.p_dec = off;
     off = align256(off + sizeof(int64_t));
     w.rows = off;

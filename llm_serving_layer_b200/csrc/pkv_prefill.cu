@@ -117,7 +117,8 @@ __global__ void __launch_bounds__(1024) prefill_plan_kernel(
   if (s_bad || s_total > max_tiles) {
     if (tid == 0) {
       flag(st, PKV_DEV_META_BAD);
-      *n_tiles = 0;
+      n_tiles[0] = 0;
+      n_tiles[1] = n_tiles[2] = 0;  // the lean prefill kernel's item claim and exit counters
       if (mixed) *mo.p_dec = 0;
     }
     __threadfence();  // p_dec is read by the decode kernel before its griddepcontrol.wait
@@ -158,7 +159,10 @@ __global__ void __launch_bounds__(1024) prefill_plan_kernel(
       tiles[pos] = make_int2(s, j0);
     }
   }
-  if (tid == 0) *n_tiles = s_total;
+  if (tid == 0) {
+    n_tiles[0] = s_total;
+    n_tiles[1] = n_tiles[2] = 0;  // the lean prefill kernel's item claim and exit counters
+  }
   // the tcgen05 prefill kernel reads the tile list before its griddepcontrol.wait
   // (it starts only once this kernel has completed): stores visible at GPU scope
   __threadfence();

@@ -84,6 +84,7 @@ struct TcArgs {
   int n_seqs, n_tokens, n_heads, n_kv, layer;
   float scale_log2;
   int early_ctas;  // CTAs [0, early_ctas) are the first wave: they read the plan before griddepcontrol.wait
+  int32_t* claim;  // [2] the lean kernel's next item to claim and CTAs finished (zeroed by the plan kernel)
 };
 
 // ---------------------------------------------------------------- tcgen05 helpers
@@ -977,12 +978,539 @@ __global__ void __launch_bounds__(TC_THREADS, 2) prefill_tc_persistent_kernel(
 
 size_t tcp_smem() { return 1024 + 2 * size_t(TC_QTILE) + size_t(TC_NST) * TC_STAGE + 256; }
 
+// ------------------------------------------------------------------ lean kernel
+// prefill_tc_lean_kernel: the persistent kernel's item walk with three CTAs
+// per SM instead of two, so that each SM sub-partition interleaves three
+// softmax warps' block chains instead of two. What buys the residency: 128
+// TMEM columns per CTA (one S block and one O) and P in shared memory instead
+// of tensor memory. With P out of the S columns, the next block's S MMA may
+// overwrite S as soon as the softmax threads have loaded it into registers:
+// S_{j+1} is computed while the softmax of block j runs, as with two S
+// buffers. Shared memory (67 KiB): the query tile, K and V rings of two
+// 64-key slots each, and the P tile ([128 rows][64 keys], 128B swizzle, the
+// A operand of the P.V MMA). K and V have rings of their own because a K slot
+// is free once its block's S MMA completed, a softmax period before the
+// block's P.V frees the V slot: the producer loads K two blocks ahead of the
+// S MMA that needs it, and the page ids of a block are read before its slots
+// are waited for.
+// Per block j the softmax threads wait for S_j, load it, release it, find
+// the row maximum, wait for P.V_{j-1} (the P tile is free again and O holds
+// every earlier block), write P_j and rescale O if needed; the MMA warp
+// issues S_{j+1} once S_j is released and K_{j+1} landed, and P.V_j once P_j
+// and V_j landed.
+constexpr int TL_MINB = 3;          // CTAs per SM
+constexpr int TL_NST = 2;           // slots of the K ring and of the V ring
+constexpr int TL_TMEM_COLS = 128;   // S in columns 0-63, O in 64-127
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};\n\t"
+      "tcgen05.wait::st.sync.aligned;" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+
+// O row *= alpha (the lazy rescale; rare): out of line, so that the registers
+// it needs are saved on its own path and not reserved in the block loop.
+__device__ __noinline__ void tl_rescale_o(uint32_t tO, float alpha) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint32_t o[16];
+    tmem_ld16(tO + q * 16, o);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+    tmem_st16(tO + q * 16, o);
+  }
+}
+
+// exp2(s * sc - mu) of a row's 64 scores, packed to pairs of the pool dtype
+// and stored as the row of P in shared memory (16-byte chunk c of row r at
+// r * 128 + ((c ^ (r & 7)) << 4): the 128B swizzle of a K-major operand); the
+// sum of the exponentials is added to `l`.
+template <typename T>
+__device__ __forceinline__ void tl_exp64_smem(const uint32_t (&s)[64], unsigned long long sc2,
+                                              unsigned long long nmu2, float& l, unsigned char* prow, int r) {
+  unsigned long long lt2[2] = {0ull, 0ull};
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    uint32_t pk[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int e = c * 8 + 2 * i;
+      float x0, x1;
+      f32x2_split(fma_f32x2(f32x2(__uint_as_float(s[e]), __uint_as_float(s[e + 1])), sc2, nmu2), x0, x1);
+      const float p0 = ex2(x0), p1 = ex2(x1);
+      lt2[i & 1] = add_f32x2(lt2[i & 1], f32x2(p0, p1));
+      pk[i] = MmaOp<T>::pack(p0, p1);
+    }
+    *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+  }
+  float a0, a1, b0, b1;
+  f32x2_split(lt2[0], a0, a1);
+  f32x2_split(lt2[1], b0, b1);
+  l += (a0 + a1) + (b0 + b1);
+}
+
+// A CTA of the lean kernel is done with the claim counter: the last one of
+// the launch zeroes both counters for the next launch with the same plan
+// (which claims only after its griddepcontrol.wait, i.e. after this launch
+// completed).
+__device__ __forceinline__ void tl_count_exit(int32_t* claim) {
+  __threadfence();
+  if (atomicAdd(claim + 1, 1) == int(gridDim.x) - 1) {
+    claim[0] = 0;
+    claim[1] = 0;
+    __threadfence();
+  }
+}
+
+// An item's fields as the lean kernel's producer publishes them (nblk = 0:
+// no more items; zero: a page id outside the pool, the item's rows are zeros).
+struct TlItem {
+  int h, q0, j0, ql, kv, npages, lpl, n_pg, nblk, zero;
+};
+
+template <typename T, int G>
+__global__ void __launch_bounds__(TC_THREADS, TL_MINB) prefill_tc_lean_kernel(
+    const __grid_constant__ CUtensorMap tmap, const __grid_constant__ CUtensorMap qmap, const TcArgs a) {
+  constexpr int TPT = TC_ROWS / G;  // tokens per tile
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char* qbuf = smem;                             // [128 rows][128 B], 128B swizzle
+  unsigned char* kst = smem + TC_QTILE;                   // TL_NST x K [64 keys][128 B]
+  unsigned char* vst = kst + size_t(TL_NST) * TC_KTILE;   // TL_NST x V [64 keys][128 B]
+  unsigned char* pbuf = vst + size_t(TL_NST) * TC_KTILE;  // P [128 rows][128 B], 128B swizzle
+  uint64_t* kfull = reinterpret_cast<uint64_t*>(pbuf + TC_QTILE);
+  uint64_t* kempty = kfull + TL_NST;  // S of the slot's block completed
+  uint64_t* vfull = kempty + TL_NST;
+  uint64_t* vempty = vfull + TL_NST;  // P.V of the slot's block completed
+  uint64_t* s_full = vempty + TL_NST; // S block in TMEM
+  uint64_t* s_free = s_full + 1;      // S loaded by the softmax threads, 128 arrivals
+  uint64_t* p_full = s_free + 1;      // P in shared memory (and O rescaled), 128 arrivals
+  uint64_t* pv_done = p_full + 1;     // P.V of the block completed (P tile free, O updated)
+  uint64_t* q_full = pv_done + 1;     // query tile landed (TMA)
+  uint64_t* q_empty = q_full + 1;     // the item's S MMAs read the query tile
+  uint64_t* o_free = q_empty + 1;     // epilogue read O, 128 arrivals
+  uint64_t* item_full = o_free + 1;   // [2] the producer published the item's fields
+  uint64_t* item_empty = item_full + 2;  // [2] the MMA warp and the softmax threads are done with them, 129 arrivals
+  uint64_t* drain = item_empty + 2;   // every MMA of the CTA completed
+  __shared__ uint32_t s_tmem;
+  __shared__ TlItem s_item[2];        // the items, in the order every role walks them
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_trigger();
+  // The plan kernel (tile list) completed before this kernel could start and
+  // fenced its stores: the item count may be read before griddepcontrol.wait.
+  const int n_items = __ldcg(a.n_tiles) * a.n_kv;
+  if (int(blockIdx.x) >= n_items) {  // no item for this CTA (uniform over the CTA)
+    pdl_wait();                      // the counters belong to the previous launch until it completed
+    if (threadIdx.x == 0) tl_count_exit(a.claim);
+    return;
+  }
+
+  if (threadIdx.x == 0) {
+    prefetch_tmap(&tmap);
+    prefetch_tmap(&qmap);
+    for (int i = 0; i < TL_NST; ++i) {
+      mbar_init(&kfull[i], 1);
+      mbar_init(&kempty[i], 1);
+      mbar_init(&vfull[i], 1);
+      mbar_init(&vempty[i], 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(s_free, 128);
+    mbar_init(p_full, 128);
+    mbar_init(pv_done, 1);
+    mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
+    mbar_init(o_free, 128);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&item_full[i], 1);
+      mbar_init(&item_empty[i], 129);
+    }
+    mbar_init(drain, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane < 2 * TC_PPB) {
+    // warm L2 with this head's slices of the first item's first two key blocks:
+    // a hint (no shared memory written), so it may run before the wait
+    const TcItem f = tc_item<TPT>(a, int(blockIdx.x), true);
+    if (!f.bad && lane < f.n_pg) {
+      const int id = __ldcg(a.kv_indices + f.pa + lane);
+      if (id >= 0 && id < a.num_blocks) {
+        tma_prefetch_l2_4d(&tmap, 0, id * TC_P, f.h, 2 * a.layer);
+        tma_prefetch_l2_4d(&tmap, 0, id * TC_P, f.h, 2 * a.layer + 1);
+      }
+    }
+  }
+  // ---- tensor memory: 128 columns S | O, freed on every path below
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
+                 "r"(TL_TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = s_tmem;
+  const uint32_t tO = tbase + TC_KB;
+  pdl_wait();  // q and this layer's appended K/V rows are written by earlier kernels
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    // Walks the items, checks each one's page ids (all lanes) and publishes its
+    // fields in the two-slot item ring, then (lane 0) loads its query tile and
+    // its K/V blocks.
+    const int kvc = 2 * a.layer;
+    uint32_t kiss = 0, viss = 0;  // K / V slots filled so far (global key-block counters)
+    int it = 0;                   // items published
+    bool dead = false;
+    while (!dead) {
+      // items are claimed from the front of the longest-first list as CTAs
+      // become free (the counter was zeroed by the plan kernel or by the last
+      // CTA of the previous launch, which completed before griddepcontrol.wait)
+      int w = 0;
+      if (lane == 0) w = atomicAdd(a.claim, 1);
+      w = __shfl_sync(0xffffffffu, w, 0);
+      const bool end = w >= n_items;
+      TcItem I{};
+      if (!end) {
+        I = tc_item<TPT>(a, w, false);
+        if (I.bad) {
+          if (lane == 0) flag(a.st, PKV_DEV_META_BAD);
+          continue;
+        }
+      }
+      bool pg_bad = false;
+      for (int pg = lane; pg < I.n_pg; pg += 32) {
+        const int id = a.kv_indices[I.pa + pg];
+        pg_bad |= id < 0 || id >= a.num_blocks;
+      }
+      pg_bad = __any_sync(0xffffffffu, pg_bad);
+      const int sl = it & 1;
+      // the slot is free once every consumer is done with the item two back
+      if (it >= 2 && !mbar_wait_bounded_sleepy(&item_empty[sl], ((it - 2) >> 1) & 1, a.st, 32)) dead = true;
+      dead = __any_sync(0xffffffffu, dead);
+      if (dead) break;
+      if (lane == 0) {
+        TlItem& o = s_item[sl];
+        o.h = I.h;
+        o.q0 = I.q0;
+        o.j0 = I.j0;
+        o.ql = I.ql;
+        o.kv = I.kv;
+        o.npages = I.npages;
+        o.lpl = I.lpl;
+        o.n_pg = I.n_pg;
+        o.nblk = end ? 0 : I.nblk;  // 0: no more items
+        o.zero = pg_bad ? 1 : 0;
+        if (pg_bad) flag(a.st, PKV_DEV_SLOT_OOB);
+        mbar_arrive(&item_full[sl]);
+      }
+      __syncwarp();
+      if (end) break;
+      if (lane == 0) {
+        if (it >= 1 && !mbar_wait_bounded_sleepy(q_empty, (it - 1) & 1, a.st, 64)) dead = true;
+        if (!dead) {
+          mbar_arrive_expect_tx(q_full, TC_QTILE);
+          tma_load_3d(qbuf, &qmap, q_full, 0, I.h * G, I.q0 + I.j0);
+        }
+        for (int j = 0; j < I.nblk && !dead; ++j) {
+          int rows[TC_PPB];
+#pragma unroll
+          for (int u = 0; u < TC_PPB; ++u) {
+            const int pg = j * TC_PPB + u;
+            // a page past the tile's visible keys reads the zero fill of a negative coordinate
+            rows[u] = pg < I.n_pg ? a.kv_indices[I.pa + pg] * TC_P : -TC_P;
+          }
+          const int st = int(kiss % TL_NST);
+          if (kiss >= TL_NST && !mbar_wait_bounded_sleepy(&kempty[st], ((kiss / TL_NST) - 1) & 1, a.st, 32)) {
+            dead = true;
+            break;
+          }
+          mbar_arrive_expect_tx(&kfull[st], TC_KTILE);
+#pragma unroll
+          for (int u = 0; u < TC_PPB; ++u)
+            tma_load_4d(kst + size_t(st) * TC_KTILE + u * TC_PAGE, &tmap, &kfull[st], 0, rows[u], I.h, kvc);
+          ++kiss;
+          if (viss >= TL_NST && !mbar_wait_bounded_sleepy(&vempty[st], ((viss / TL_NST) - 1) & 1, a.st, 32)) {
+            dead = true;
+            break;
+          }
+          mbar_arrive_expect_tx(&vfull[st], TC_KTILE);
+#pragma unroll
+          for (int u = 0; u < TC_PPB; ++u)
+            tma_load_4d(vst + size_t(st) * TC_KTILE + u * TC_PAGE, &tmap, &vfull[st], 0, rows[u], I.h, kvc + 1);
+          ++viss;
+        }
+      }
+      dead = __shfl_sync(0xffffffffu, dead, 0);
+      ++it;
+    }
+    if (dead && lane == 0) {
+      // let this CTA's own copies land before its shared memory can be released
+      for (uint32_t i = kiss > TL_NST ? kiss - TL_NST : 0; i < kiss; ++i)
+        mbar_wait_bounded(&kfull[i % TL_NST], (i / TL_NST) & 1, nullptr);
+      for (uint32_t i = viss > TL_NST ? viss - TL_NST : 0; i < viss; ++i)
+        mbar_wait_bounded(&vfull[i % TL_NST], (i / TL_NST) & 1, nullptr);
+      if (it >= 1) mbar_wait_bounded(q_full, (it - 1) & 1, nullptr);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    constexpr int fmt = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
+    constexpr uint32_t idS = idesc_f16(fmt, 0, TC_KB);
+    constexpr uint32_t idPV = idesc_f16(fmt, 1, TC_D);
+    const uint32_t q_addr = smem_u32(qbuf), p_addr = smem_u32(pbuf);
+    uint32_t g = 0;
+    int it = 0;
+    bool dead = false;
+    // P.V of global block gp (the item's block jp), after its P and its V
+    // slot landed; the item's first P.V overwrites O, which the previous
+    // item's epilogue reads
+    auto pv = [&](uint32_t gp, int jp, const TlItem& I) -> bool {
+      const int stp = int(gp % TL_NST);
+      bool bad = !mbar_wait_bounded(p_full, gp & 1, a.st);
+      if (!bad && jp == 0 && it >= 1 && !mbar_wait_bounded(o_free, (it - 1) & 1, a.st)) bad = true;
+      if (!bad && !mbar_wait_bounded(&vfull[stp], (gp / TL_NST) & 1, a.st)) bad = true;
+      bad = __any_sync(0xffffffffu, bad);
+      if (bad) return false;
+      if (jp == (I.npages - 1) / TC_PPB && I.lpl < TC_P && I.npages - 1 < I.n_pg) {
+        // rows lpl..15 of the last page's V slice were never written: zero them
+        uint4* vt = reinterpret_cast<uint4*>(vst + size_t(stp) * TC_KTILE + (I.npages - 1 - jp * TC_PPB) * TC_PAGE);
+        for (int rr = I.lpl * 8 + lane; rr < TC_P * 8; rr += 32) vt[rr] = make_uint4(0u, 0u, 0u, 0u);
+        fence_proxy_async_smem();
+        __syncwarp();
+      }
+      if (lane == 0) {
+        tc_fence_after();
+        const uint32_t vaddr = smem_u32(vst + size_t(stp) * TC_KTILE);
+#pragma unroll
+        for (int kk = 0; kk < TC_KB / 16; ++kk)
+          umma_ss(tO, sw128_desc(p_addr + 32 * kk), sw128_desc(vaddr + 16 * 128 * kk), idPV,
+                  (jp > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(&vempty[stp]);
+        umma_commit(pv_done);
+      }
+      __syncwarp();
+      return true;
+    };
+    while (!dead) {
+      const int sl = it & 1;
+      if (!mbar_wait_bounded(&item_full[sl], (it >> 1) & 1, a.st)) dead = true;
+      dead = __any_sync(0xffffffffu, dead);
+      if (dead) break;
+      const TlItem I = s_item[sl];
+      if (I.nblk == 0) break;
+      if (!mbar_wait_bounded(q_full, it & 1, a.st)) dead = true;
+      dead = __any_sync(0xffffffffu, dead);
+      if (dead) break;
+      for (int j = 0; j < I.nblk; ++j) {
+        const uint32_t gj = g + j;
+        const int st = int(gj % TL_NST);
+        // S_j overwrites S_{j-1}: after the softmax threads loaded it
+        if (gj >= 1 && !mbar_wait_bounded(s_free, (gj - 1) & 1, a.st)) dead = true;
+        if (!dead && !mbar_wait_bounded(&kfull[st], (gj / TL_NST) & 1, a.st)) dead = true;
+        dead = __any_sync(0xffffffffu, dead);
+        if (dead) break;
+        if (lane == 0) {
+          tc_fence_after();
+          const uint32_t kaddr = smem_u32(kst + size_t(st) * TC_KTILE);
+#pragma unroll
+          for (int kk = 0; kk < TC_D / 16; ++kk)
+            umma_ss(tbase, sw128_desc(q_addr + 32 * kk), sw128_desc(kaddr + 32 * kk), idS, kk > 0);
+          umma_commit(s_full);
+          umma_commit(&kempty[st]);
+          if (j == I.nblk - 1) umma_commit(q_empty);  // the item's last read of its query tile
+        }
+        __syncwarp();
+        if (j >= 1 && !pv(gj - 1, j - 1, I)) {
+          dead = true;
+          break;
+        }
+      }
+      if (dead) break;
+      if (!pv(g + I.nblk - 1, I.nblk - 1, I)) {
+        dead = true;
+        break;
+      }
+      if (lane == 0) mbar_arrive(&item_empty[sl]);
+      g += I.nblk;
+      ++it;
+    }
+    // every MMA issued above has completed before TMEM is freed
+    if (lane == 0) {
+      umma_commit(drain);
+      mbar_wait_bounded(drain, 0, a.st);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ softmax warps
+    const int q4 = warp & 3;       // TMEM lane quarter this warp may access
+    const int r = q4 * 32 + lane;  // this thread's row: token r / G, query head r % G of the item's group
+    const uint32_t lane_off = uint32_t(q4 * 32) << 16;
+    const float sl2 = a.scale_log2;
+    const float sc = sl2 > 0.f ? sl2 : 1.f;  // the scale still to apply after masking (log2 units)
+    unsigned char* prow = pbuf + r * 128;
+    T* out = static_cast<T*>(a.out);
+    uint32_t g = 0;
+    int it = 0;
+    bool dead = false;
+    while (!dead) {
+      const int sl = it & 1;
+      if (!mbar_wait_bounded(&item_full[sl], (it >> 1) & 1, a.st)) dead = true;
+      dead = __any_sync(0xffffffffu, dead);
+      if (dead) break;
+      const TlItem I = s_item[sl];
+      if (I.nblk == 0) break;
+      const int jw0 = I.j0, qlw = I.ql, q0w = I.q0, hw = I.h;  // for the epilogue's stores
+      const int jq = I.j0 + r / G;
+      const bool valid = jq < I.ql;
+      const int lim = valid ? I.kv - I.ql + jq : -1;  // last visible key of this row
+      float m = -INFINITY, l = 0.f;
+      for (int j = 0; j < I.nblk; ++j) {
+        const uint32_t gj = g + j;
+        if (!mbar_wait_bounded(s_full, gj & 1, a.st)) dead = true;
+        dead = __any_sync(0xffffffffu, dead);
+        if (dead) break;
+        tc_fence_after();
+        uint32_t sr[64];
+        tmem_ld64(tbase + lane_off, sr);
+        tc_fence_before();
+        mbar_arrive(s_free);  // S_{j+1} may overwrite S now
+        const int kb0 = j * TC_KB;
+        if (sl2 <= 0.f) {  // a non-positive scale: scale first so the masked -inf stays the minimum
+#pragma unroll
+          for (int i = 0; i < 64; ++i) sr[i] = __float_as_uint(__uint_as_float(sr[i]) * sl2);
+        }
+        if (kb0 + TC_KB - 1 > lim) {  // the block reaches past this row's last visible key
+#pragma unroll
+          for (int i = 0; i < 64; ++i)
+            if (kb0 + i > lim) sr[i] = __float_as_uint(-INFINITY);
+        }
+        float mx;
+        {
+          float t[8];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) t[u] = __uint_as_float(sr[u]);
+#pragma unroll
+          for (int i = 8; i < 64; i += 2)
+            t[(i >> 1) & 7] = max3f(t[(i >> 1) & 7], __uint_as_float(sr[i]), __uint_as_float(sr[i + 1]));
+          mx = max3f(max3f(t[0], t[1], t[2]), max3f(t[3], t[4], t[5]), fmaxf(t[6], t[7]));
+        }
+        mx = mx * sc;  // -inf stays -inf (sc > 0)
+        const float mn = fmaxf(m, mx);
+        float m_new = m;
+        if (mn != -INFINITY && (m == -INFINITY || mn > m + TC_RESCALE)) m_new = mn;
+        const bool resc = (m_new != m) && (m != -INFINITY);  // earlier blocks already added to O
+        const float alpha = resc ? ex2(m - m_new) : 1.f;
+        l *= alpha;
+        m = m_new;
+        // P.V_{j-1} done: the P tile is free and O holds every earlier block
+        if (gj >= 1 && !mbar_wait_bounded(pv_done, (gj - 1) & 1, a.st)) dead = true;
+        dead = __any_sync(0xffffffffu, dead);
+        if (dead) break;
+        const float mu = m == -INFINITY ? 0.f : m;
+        tl_exp64_smem<T>(sr, f32x2(sc, sc), f32x2(-mu, -mu), l, prow, r);
+        fence_proxy_async_smem();  // P (generic-proxy stores) -> the P.V MMA (async proxy)
+        if (__any_sync(0xffffffffu, resc)) {
+          tc_fence_after();
+          tl_rescale_o(tO + lane_off, alpha);
+        }
+        tc_fence_before();
+        mbar_arrive(p_full);
+      }
+      if (dead) break;
+      // ---- epilogue: O / l of the item -> global memory, then O is released
+      // to the next item's first P.V. The rows are staged in this warp's own
+      // rows of the P tile (P.V of the item's last block completed, and no
+      // other warp writes them), then stored as runs of four whole rows
+      // (512 bytes for G = 4: one token's query heads of this KV head).
+      const uint32_t gl = g + I.nblk - 1;
+      if (!mbar_wait_bounded(pv_done, gl & 1, a.st)) dead = true;
+      dead = __any_sync(0xffffffffu, dead);
+      if (dead) break;
+      tc_fence_after();
+      const float inv = (l > 0.f && !I.zero) ? 1.f / l : 0.f;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint32_t o[16];
+        tmem_ld16(tO + lane_off + q * 16, o);
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          const int e = c * 8;
+          uint4 v;
+          v.x = MmaOp<T>::pack(__uint_as_float(o[e]) * inv, __uint_as_float(o[e + 1]) * inv);
+          v.y = MmaOp<T>::pack(__uint_as_float(o[e + 2]) * inv, __uint_as_float(o[e + 3]) * inv);
+          v.z = MmaOp<T>::pack(__uint_as_float(o[e + 4]) * inv, __uint_as_float(o[e + 5]) * inv);
+          v.w = MmaOp<T>::pack(__uint_as_float(o[e + 6]) * inv, __uint_as_float(o[e + 7]) * inv);
+          if (I.zero) v = make_uint4(0u, 0u, 0u, 0u);  // a page id outside the pool: the item's rows are zeros
+          *reinterpret_cast<uint4*>(prow + (((q * 2 + c) ^ (r & 7)) << 4)) = v;
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(o_free);
+      mbar_arrive(&item_empty[sl]);  // this thread has read every field of the item it uses below
+      __syncwarp();
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        const int rw = q4 * 32 + 4 * kk + (lane >> 3);  // tile row; chunk lane % 8 of it
+        const int ch = lane & 7;
+        const int tok = jw0 + rw / G;
+        if (tok < qlw) {
+          const uint4 v = *reinterpret_cast<const uint4*>(pbuf + rw * 128 + ((ch ^ (rw & 7)) << 4));
+          reinterpret_cast<uint4*>(out + ((int64_t(q0w) + tok) * a.n_heads + hw * G + rw % G) * TC_D)[ch] = v;
+        }
+      }
+      __syncwarp();  // the next item's P rows of this warp are written after these reads
+      g += I.nblk;
+      ++it;
+    }
+  }
+
+  // ---- free tensor memory once every role is done with it
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tbase), "r"(TL_TMEM_COLS)
+                 : "memory");
+  }
+  if (threadIdx.x == 0) tl_count_exit(a.claim);
+}
+
+size_t tl_smem() { return 1024 + 2 * size_t(TC_QTILE) + size_t(2 * TL_NST) * TC_KTILE + 256; }
+
 // Which launches the persistent kernel takes: PKV_PREFILL_PERSISTENT unset or 1
 // = launches of more than one wave of CTAs, 0 = none (one CTA per tile for every
 // launch), 2 = every launch (for tests of the persistent kernel on small batches).
 int prefill_persistent_mode() {
   static const int mode = [] {
     const char* e = getenv("PKV_PREFILL_PERSISTENT");
+    if (e && e[0] == '0') return 0;
+    if (e && e[0] == '2') return 2;
+    return 1;
+  }();
+  return mode;
+}
+
+// Which persistent kernel runs: PKV_PREFILL_LEAN unset or 1 = the lean kernel
+// (three CTAs per SM) for launches of more than one wave, 0 = the two-CTA
+// persistent kernel, 2 = the lean kernel for every launch (tests).
+int prefill_lean_mode() {
+  static const int mode = [] {
+    const char* e = getenv("PKV_PREFILL_LEAN");
     if (e && e[0] == '0') return 0;
     if (e && e[0] == '2') return 2;
     return 1;
@@ -1018,11 +1546,12 @@ int q_tmap(int32_t dtype, const void* q, int n_tokens, int n_heads, int groups, 
 }
 
 
-// Launches one of the two kernels: `qm` == nullptr -> one CTA per (tile, KV
-// head) (prefill_tc_kernel), otherwise the persistent kernel over `grid` CTAs.
+// Launches one of the three kernels: `qm` == nullptr -> one CTA per (tile, KV
+// head) (prefill_tc_kernel), otherwise a persistent kernel over `grid` CTAs:
+// prefill_tc_lean_kernel when `lean`, else prefill_tc_persistent_kernel.
 template <typename T, int G>
-int launch_tc_t(const pkv_pool& p, const CUtensorMap& tm, const CUtensorMap* qm, const TcArgs& a, int grid,
-                cudaStream_t s) {
+int launch_tc_t(const pkv_pool& p, const CUtensorMap& tm, const CUtensorMap* qm, bool lean, const TcArgs& a,
+                int grid, cudaStream_t s) {
   static std::mutex mu;
   static std::vector<char> ready;
   int dev = 0;
@@ -1035,10 +1564,18 @@ int launch_tc_t(const pkv_pool& p, const CUtensorMap& tm, const CUtensorMap* qm,
                                         int(tc_smem())));
       PKV_CUDA_RET(cudaFuncSetAttribute(prefill_tc_persistent_kernel<T, G>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, int(tcp_smem())));
+      PKV_CUDA_RET(cudaFuncSetAttribute(prefill_tc_lean_kernel<T, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        int(tl_smem())));
+      // three CTAs of ~67 KiB need the whole shared-memory carveout
+      PKV_CUDA_RET(cudaFuncSetAttribute(prefill_tc_lean_kernel<T, G>,
+                                        cudaFuncAttributePreferredSharedMemoryCarveout, int(cudaSharedmemCarveoutMaxShared)));
       ready[dev] = 1;
     }
   }
-  if (qm)
+  if (qm && lean)
+    PKV_CUDA_RET(launch_kernel(prefill_tc_lean_kernel<T, G>, dim3(grid), dim3(TC_THREADS), tl_smem(), s, true, tm,
+                               *qm, a));
+  else if (qm)
     PKV_CUDA_RET(launch_kernel(prefill_tc_persistent_kernel<T, G>, dim3(grid), dim3(TC_THREADS), tcp_smem(), s,
                                true, tm, *qm, a));
   else
@@ -1047,13 +1584,13 @@ int launch_tc_t(const pkv_pool& p, const CUtensorMap& tm, const CUtensorMap* qm,
 }
 
 template <typename T>
-int launch_tc_g(const pkv_pool& p, int groups, const CUtensorMap& tm, const CUtensorMap* qm, const TcArgs& a,
-                int grid, cudaStream_t s) {
+int launch_tc_g(const pkv_pool& p, int groups, const CUtensorMap& tm, const CUtensorMap* qm, bool lean,
+                const TcArgs& a, int grid, cudaStream_t s) {
   switch (groups) {
-    case 1: return launch_tc_t<T, 1>(p, tm, qm, a, grid, s);
-    case 2: return launch_tc_t<T, 2>(p, tm, qm, a, grid, s);
-    case 4: return launch_tc_t<T, 4>(p, tm, qm, a, grid, s);
-    case 8: return launch_tc_t<T, 8>(p, tm, qm, a, grid, s);
+    case 1: return launch_tc_t<T, 1>(p, tm, qm, lean, a, grid, s);
+    case 2: return launch_tc_t<T, 2>(p, tm, qm, lean, a, grid, s);
+    case 4: return launch_tc_t<T, 4>(p, tm, qm, lean, a, grid, s);
+    case 8: return launch_tc_t<T, 8>(p, tm, qm, lean, a, grid, s);
   }
   return fail(PKV_ERR_UNSUPPORTED, "tcgen05 prefill kernel: unsupported GQA group size");
 }
@@ -1089,6 +1626,7 @@ int prefill_tc_attend(const pkv_pool& p, int layer, int n_heads, const void* q, 
   a.layer = layer;
   a.scale_log2 = scale * 1.4426950408889634f;
   a.early_ctas = 2 * num_sms();  // two CTAs per SM (__launch_bounds__ and shared memory)
+  a.claim = const_cast<int32_t*>(n_tiles) + 1;  // the plan's workspace: n_tiles[1..2]
   const int qt = prefill_tc_tile_tokens(n_heads, p.n_kv_heads);
   const int64_t bound = std::min<int64_t>((int64_t(b.n_tokens) + qt - 1) / qt + b.n_seqs, tiles_cap);
   const int64_t items = std::max<int64_t>(1, bound) * p.n_kv_heads;
@@ -1097,17 +1635,18 @@ int prefill_tc_attend(const pkv_pool& p, int layer, int n_heads, const void* q, 
   CUtensorMap qm;
   const CUtensorMap* qmp = nullptr;
   int64_t grid = items;
-  const int mode = prefill_persistent_mode();
-  if ((mode == 1 && items > slots) || mode == 2) {
+  const int mode = prefill_persistent_mode(), lean_mode = prefill_lean_mode();
+  const bool lean = lean_mode == 2 || (lean_mode == 1 && mode == 1 && items > slots);
+  if ((mode == 1 && items > slots) || mode == 2 || lean) {
     // more tiles than one wave: persistent CTAs walk the tiles (each CTA's
     // setup, query loads and epilogues overlap its other tiles' work)
     if (int rc = q_tmap(p.dtype, q, b.n_tokens, n_heads, groups, &qm)) return rc;
     qmp = &qm;
-    grid = std::min(items, slots);
+    grid = std::min(items, lean ? int64_t(TL_MINB) * num_sms() : slots);
   }
   if (grid > 0x7fffffff) return fail(PKV_ERR_ARG, "prefill batch too large for one launch");
-  if (p.dtype == PKV_F16) return launch_tc_g<__half>(p, groups, tm, qmp, a, int(grid), s);
-  return launch_tc_g<__nv_bfloat16>(p, groups, tm, qmp, a, int(grid), s);
+  if (p.dtype == PKV_F16) return launch_tc_g<__half>(p, groups, tm, qmp, lean, a, int(grid), s);
+  return launch_tc_g<__nv_bfloat16>(p, groups, tm, qmp, lean, a, int(grid), s);
 }
 
 }  // namespace pkv

@@ -1,19 +1,23 @@
 """
-The two tcgen05 prefill kernels against each other's paths and the oracle.
+The three tcgen05 prefill kernels against each other's paths and the oracle.
 
 Launches of more than one wave of CTAs (more than two tiles x KV heads per SM)
-run the persistent kernel, smaller ones one CTA per tile. The environment
-variable ``PKV_PREFILL_PERSISTENT`` (read once per process) moves the line:
-``2`` sends every launch to the persistent kernel, ``0`` none. Here the whole
-prefill suite and the reference-scheduler trace replay run again in child
-processes under both settings, so each kernel meets every case (chunks after
-long prefixes, tile and page edges, every GQA group size, bf16, NaN-poisoned
-page tails, radix sharing with copy-on-write, mixed batches), and a large
-batch — persistent CTAs walking several tiles each — with one sequence whose
-page table points outside the pool and one whose lengths disagree checks that
-only those sequences are affected: the first gets zero rows and
-``PKV_DEV_SLOT_OOB``, the second no rows written and ``PKV_DEV_META_BAD``, and
-every other row is within the fp16 tolerance of the float64 evaluation.
+run a persistent kernel — by default the lean one (three CTAs per SM), with
+``PKV_PREFILL_LEAN=0`` the two-CTA one — and smaller launches one CTA per
+tile. The environment variables (read once per process) move the lines:
+``PKV_PREFILL_PERSISTENT=2`` sends every launch to the two-CTA persistent
+kernel, ``PKV_PREFILL_PERSISTENT=0`` none; ``PKV_PREFILL_LEAN=2`` every launch
+to the lean kernel. Here the whole prefill suite and the reference-scheduler
+trace replay run again in child processes under each setting, so each kernel
+meets every case (chunks after long prefixes, tile and page edges, every GQA
+group size, bf16, NaN-poisoned page tails, radix sharing with copy-on-write,
+mixed batches), and a large batch — persistent CTAs walking several tiles
+each — with one sequence whose page table points outside the pool and one
+whose lengths disagree checks that only those sequences are affected: the
+first gets zero rows and ``PKV_DEV_SLOT_OOB``, the second no rows written and
+``PKV_DEV_META_BAD``, and every other row is within the fp16 tolerance of the
+float64 evaluation (in this process with the default kernel, and in a child
+process with the two-CTA persistent kernel).
 """
 
 from __future__ import annotations
@@ -35,13 +39,30 @@ pytestmark = pytest.mark.gpu
 ROOT = Path(__file__).resolve().parents[1]
 
 
-@pytest.mark.parametrize("mode", ["2", "0"])
-def test_prefill_suite_under_each_kernel(mode):
-    env = dict(os.environ, PKV_PREFILL_PERSISTENT=mode)
-    r = subprocess.run([sys.executable, "-m", "pytest", "-x", "-q", "-m", "gpu", "-p", "no:cacheprovider",
-                        "tests/test_gpu_prefill.py", "tests/test_gpu_trace.py"],
+KERNELS = {
+    "persistent": {"PKV_PREFILL_PERSISTENT": "2", "PKV_PREFILL_LEAN": "0"},
+    "lean": {"PKV_PREFILL_LEAN": "2"},
+    "per_tile": {"PKV_PREFILL_PERSISTENT": "0", "PKV_PREFILL_LEAN": "0"},
+}
+
+
+def _child(env_over, *targets):
+    env = dict(os.environ, **env_over)
+    r = subprocess.run([sys.executable, "-m", "pytest", "-x", "-q", "-m", "gpu", "-p", "no:cacheprovider", *targets],
                        cwd=ROOT, env=env, capture_output=True, text=True, timeout=900)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]
+
+
+@pytest.mark.parametrize("kernel", sorted(KERNELS))
+def test_prefill_suite_under_each_kernel(kernel):
+    _child(KERNELS[kernel], "tests/test_gpu_prefill.py", "tests/test_gpu_trace.py")
+
+
+def test_two_cta_persistent_kernel_isolates_bad_sequences():
+    if os.environ.get("PKV_PREFILL_LEAN") == "0":
+        pytest.skip("this process already runs the two-CTA persistent kernel")
+    _child({"PKV_PREFILL_LEAN": "0"},
+           "tests/test_gpu_prefill_persistent.py::test_persistent_kernel_isolates_bad_sequences")
 
 
 def test_persistent_kernel_isolates_bad_sequences():
