@@ -1442,13 +1442,14 @@ __global__ void __launch_bounds__(TC_THREADS, TL_MINB) prefill_tc_lean_kernel(
       dead = __any_sync(0xffffffffu, dead);
       if (dead) break;
       tc_fence_after();
-      const float inv = (l > 0.f && !I.zero) ? 1.f / l : 0.f;
+      {
+        uint32_t o[64];
+        tmem_ld64(tO + lane_off, o);
+        tc_fence_before();
+        mbar_arrive(o_free);  // O read: the next item's first P.V may overwrite it
+        const float inv = (l > 0.f && !I.zero) ? 1.f / l : 0.f;
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        uint32_t o[16];
-        tmem_ld16(tO + lane_off + q * 16, o);
-#pragma unroll
-        for (int c = 0; c < 2; ++c) {
+        for (int c = 0; c < 8; ++c) {
           const int e = c * 8;
           uint4 v;
           v.x = MmaOp<T>::pack(__uint_as_float(o[e]) * inv, __uint_as_float(o[e + 1]) * inv);
@@ -1456,24 +1457,25 @@ __global__ void __launch_bounds__(TC_THREADS, TL_MINB) prefill_tc_lean_kernel(
           v.z = MmaOp<T>::pack(__uint_as_float(o[e + 4]) * inv, __uint_as_float(o[e + 5]) * inv);
           v.w = MmaOp<T>::pack(__uint_as_float(o[e + 6]) * inv, __uint_as_float(o[e + 7]) * inv);
           if (I.zero) v = make_uint4(0u, 0u, 0u, 0u);  // a page id outside the pool: the item's rows are zeros
-          *reinterpret_cast<uint4*>(prow + (((q * 2 + c) ^ (r & 7)) << 4)) = v;
+          *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) << 4)) = v;
         }
       }
-      tc_fence_before();
-      mbar_arrive(o_free);
       mbar_arrive(&item_empty[sl]);  // this thread has read every field of the item it uses below
       __syncwarp();
+      uint4 v[8];
 #pragma unroll
       for (int kk = 0; kk < 8; ++kk) {
         const int rw = q4 * 32 + 4 * kk + (lane >> 3);  // tile row; chunk lane % 8 of it
-        const int ch = lane & 7;
-        const int tok = jw0 + rw / G;
-        if (tok < qlw) {
-          const uint4 v = *reinterpret_cast<const uint4*>(pbuf + rw * 128 + ((ch ^ (rw & 7)) << 4));
-          reinterpret_cast<uint4*>(out + ((int64_t(q0w) + tok) * a.n_heads + hw * G + rw % G) * TC_D)[ch] = v;
-        }
+        v[kk] = *reinterpret_cast<const uint4*>(pbuf + rw * 128 + (((lane & 7) ^ (rw & 7)) << 4));
       }
-      __syncwarp();  // the next item's P rows of this warp are written after these reads
+      __syncwarp();  // the staged rows are read: this warp's next P rows may follow
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        const int rw = q4 * 32 + 4 * kk + (lane >> 3);
+        const int tok = jw0 + rw / G;
+        if (tok < qlw)
+          reinterpret_cast<uint4*>(out + ((int64_t(q0w) + tok) * a.n_heads + hw * G + rw % G) * TC_D)[lane & 7] = v[kk];
+      }
       g += I.nblk;
       ++it;
     }
