@@ -1081,6 +1081,8 @@ struct TlItem {
 };
 
 template <typename T, int G>
+// 96 registers a thread: three CTAs put up to five warps of 32 x 96 registers
+// on an SM sub-partition (16K registers each); 112 would fit only four
 __global__ void __launch_bounds__(TC_THREADS, TL_MINB) prefill_tc_lean_kernel(
     const __grid_constant__ CUtensorMap tmap, const __grid_constant__ CUtensorMap qmap, const TcArgs a) {
   constexpr int TPT = TC_ROWS / G;  // tokens per tile
