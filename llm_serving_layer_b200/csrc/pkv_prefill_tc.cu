@@ -199,22 +199,34 @@ __device__ __forceinline__ int tc_tile_pages(int64_t kv, int ql, int j0, int qt)
   return int((kv - ql + jl) / TC_P + 1);
 }
 
-template <typename T, int G>
-__global__ void __launch_bounds__(TC_THREADS, 2) prefill_tc_kernel(const __grid_constant__ CUtensorMap tmap,
-                                                                   const TcArgs a) {
+// One CTA per item. NG = 1: the tile's key blocks in one chain (two CTAs per
+// SM). NG = 2 (launches of at most one CTA per SM, where the longest tile's
+// chain of blocks is the launch's critical path): the blocks are split
+// between two groups of the CTA, even blocks and odd blocks, each with its own
+// MMA warp, K/V ring, S buffers and O in TMEM (columns 256 g .. 256 g + 191)
+// and softmax warpgroup; group 1 publishes its rows' (max, sum) in shared
+// memory and group 0 merges both O accumulators in the epilogue. The two
+// chains share the SM's exponential unit, which one chain leaves two thirds
+// idle.
+template <typename T, int G, int NG>
+__global__ void __launch_bounds__(NG == 1 ? TC_THREADS : 384, NG == 1 ? 2 : 1)
+    prefill_tc_kernel(const __grid_constant__ CUtensorMap tmap, const TcArgs a) {
   constexpr int TPT = TC_ROWS / G;  // tokens per tile
+  constexpr int SMW = NG == 1 ? 2 : 4;  // first softmax warp
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   unsigned char* qs = smem;                    // [128 rows][128 B], 128B swizzle
-  unsigned char* stages = smem + TC_QTILE;     // TC_NST x {K [64][128 B], V [64][128 B]}
-  uint64_t* full = reinterpret_cast<uint64_t*>(stages + size_t(TC_NST) * TC_STAGE);
-  uint64_t* empty = full + TC_NST;             // P.V of the stage's block completed
-  uint64_t* s_full = empty + TC_NST;           // [2] S block in TMEM
-  uint64_t* p_full = s_full + 2;               // [2] P in TMEM (and O rescaled), 128 arrivals
-  uint64_t* o_done = p_full + 2;               // [2] P.V of block jp done: o_done[jp & 1]
-  uint64_t* q_ready = o_done + 2;              // Q tile in shared memory, 128 arrivals
-  uint64_t* drain = q_ready + 1;               // every MMA of the CTA completed
+  unsigned char* stages = smem + TC_QTILE;     // NG x TC_NST x {K [64][128 B], V [64][128 B]}
+  uint64_t* bars = reinterpret_cast<uint64_t*>(stages + size_t(NG) * TC_NST * TC_STAGE);
+  // per group g: full[TC_NST], empty[TC_NST] (P.V of the stage's block completed),
+  // s_full[2] (S block in TMEM), p_full[2] (P in TMEM and O rescaled, 128
+  // arrivals), o_done[2] (P.V of local block jp done: o_done[jp & 1]), drain
+  constexpr int NBG = 2 * TC_NST + 7;
+  auto gbar = [&](int g) { return bars + g * NBG; };
+  uint64_t* q_ready = bars + NG * NBG;         // Q tile in shared memory, 128 arrivals
+  uint64_t* b_done = q_ready + 1;              // group 1 published (max, sum) and its O is final, 128 arrivals
+  float2* s_ml = reinterpret_cast<float2*>(b_done + 1);  // [128] group 1's (max, sum) per row
   __shared__ uint32_t s_tmem;
   __shared__ int s_bad;
 
@@ -276,13 +288,15 @@ __global__ void __launch_bounds__(TC_THREADS, 2) prefill_tc_kernel(const __grid_
     }
     pdl_wait();  // q and this layer's appended rows are written by earlier kernels
   }
-  // The softmax threads' query rows, loaded now so the loads travel while the
-  // page ids are checked (later CTAs) and the barriers and tensor memory are
-  // set up; they are stored to shared memory (swizzled) further down.
+  // The query rows, loaded by the first softmax warpgroup now so the loads
+  // travel while the page ids are checked (later CTAs) and the barriers and
+  // tensor memory are set up; they are stored to shared memory (swizzled)
+  // further down.
+  const int grp = warp >= SMW ? (warp - SMW) >> 2 : -1;  // softmax group of this warp
   const int r_sm = (warp & 3) * 32 + lane;  // a softmax thread's row
   const int jq_sm = j0 + r_sm % TPT;
   uint4 qv[8];
-  if (warp >= 2) {
+  if (grp == 0) {
     const bool qok = !bad && jq_sm < ql;
     const uint4* src = reinterpret_cast<const uint4*>(static_cast<const T*>(a.q) +
                                                        ((int64_t(q0) + (qok ? jq_sm : 0)) * a.n_heads + h * G + r_sm / TPT) * TC_D);
@@ -292,18 +306,21 @@ __global__ void __launch_bounds__(TC_THREADS, 2) prefill_tc_kernel(const __grid_
   if (!early) check_pages();
   if (threadIdx.x == 0) {
     prefetch_tmap(&tmap);
-    for (int i = 0; i < TC_NST; ++i) {
-      mbar_init(&full[i], 1);
-      mbar_init(&empty[i], 1);
+    for (int g = 0; g < NG; ++g) {
+      uint64_t* b = gbar(g);
+      for (int i = 0; i < TC_NST; ++i) {
+        mbar_init(&b[i], 1);            // full
+        mbar_init(&b[TC_NST + i], 1);   // empty
+      }
+      for (int i = 0; i < 2; ++i) {
+        mbar_init(&b[2 * TC_NST + i], 1);      // s_full
+        mbar_init(&b[2 * TC_NST + 2 + i], 128);  // p_full
+        mbar_init(&b[2 * TC_NST + 4 + i], 1);  // o_done
+      }
+      mbar_init(&b[2 * TC_NST + 6], 1);  // drain
     }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 128);
-    }
-    mbar_init(&o_done[0], 1);
-    mbar_init(&o_done[1], 1);
     mbar_init(q_ready, 128);
-    mbar_init(drain, 1);
+    mbar_init(b_done, 128);
     fence_mbar_init();
   }
   __syncthreads();
@@ -316,17 +333,17 @@ __global__ void __launch_bounds__(TC_THREADS, 2) prefill_tc_kernel(const __grid_
   };
   if (s_bad) {  // before any TMA or TMEM use
     if (threadIdx.x == 0) flag(a.st, s_bad == 1 ? PKV_DEV_META_BAD : PKV_DEV_SLOT_OOB);
-    if (s_bad == 2 && warp >= 2) {
-      if (T* o = out_row((warp & 3) * 32 + lane))
+    if (s_bad == 2 && grp == 0) {
+      if (T* o = out_row(r_sm))
         for (int c = 0; c < 8; ++c) reinterpret_cast<uint4*>(o)[c] = make_uint4(0u, 0u, 0u, 0u);
     }
     return;
   }
 
-  // ---- tensor memory: 256 columns (S0, S1, O), freed on every path below
+  // ---- tensor memory: 256 columns per group (S0, S1, O), freed on every path below
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
-                 "r"(TC_TMEM_COLS)
+                 "r"(TC_TMEM_COLS * NG)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -334,7 +351,8 @@ __global__ void __launch_bounds__(TC_THREADS, 2) prefill_tc_kernel(const __grid_
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = s_tmem;
-  const uint32_t tO = tbase + 128;
+  // local blocks of group g: global blocks g, g + NG, g + 2 NG, ...
+  auto nb_of = [&](int g) { return nblk > g ? (nblk - g + NG - 1) / NG : 0; };
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
@@ -343,55 +361,70 @@ __global__ void __launch_bounds__(TC_THREADS, 2) prefill_tc_kernel(const __grid_
       int issued = 0;
       bool dead = false;
       for (int j = 0; j < nblk; ++j) {
-        const int st = j % TC_NST;
-        if (j >= TC_NST && !mbar_wait_bounded_sleepy(&empty[st], ((j / TC_NST) - 1) & 1, a.st, 64)) {
+        const int g = j % NG, jj = j / NG, st = jj % TC_NST;
+        uint64_t* b = gbar(g);
+        if (jj >= TC_NST && !mbar_wait_bounded_sleepy(&b[TC_NST + st], ((jj / TC_NST) - 1) & 1, a.st, 64)) {
           dead = true;
           break;
         }
-        unsigned char* kd = stages + size_t(st) * TC_STAGE;
-        mbar_arrive_expect_tx(&full[st], TC_STAGE);
+        unsigned char* kd = stages + (size_t(g) * TC_NST + st) * TC_STAGE;
+        mbar_arrive_expect_tx(&b[st], TC_STAGE);
 #pragma unroll
         for (int u = 0; u < TC_PPB; ++u) {
           const int pg = j * TC_PPB + u;
           // a page past the tile's visible keys reads the zero fill of a negative coordinate
           const int row = pg < n_pg ? a.kv_indices[pa + pg] * TC_P : -TC_P;
-          tma_load_4d(kd + u * TC_PAGE, &tmap, &full[st], 0, row, h, kvc);
-          tma_load_4d(kd + TC_KTILE + u * TC_PAGE, &tmap, &full[st], 0, row, h, kvc + 1);
+          tma_load_4d(kd + u * TC_PAGE, &tmap, &b[st], 0, row, h, kvc);
+          tma_load_4d(kd + TC_KTILE + u * TC_PAGE, &tmap, &b[st], 0, row, h, kvc + 1);
         }
         issued = j + 1;
       }
       // let this CTA's own copies land before its shared memory can be released
       if (dead)
-        for (int i = max(0, issued - TC_NST); i < issued; ++i)
-          mbar_wait_bounded(&full[i % TC_NST], (i / TC_NST) & 1, nullptr);
+        for (int i = max(0, issued - NG * TC_NST); i < issued; ++i) {
+          const int g = i % NG, ii = i / NG;
+          mbar_wait_bounded(&gbar(g)[ii % TC_NST], (ii / TC_NST) & 1, nullptr);
+        }
     }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
+  } else if (warp >= 1 && warp <= NG) {
+    // ------------------------------------------------------------ MMA issuer of group warp - 1
+    const int g = warp - 1;
+    uint64_t* b = gbar(g);
+    uint64_t* full = b;
+    uint64_t* empty = b + TC_NST;
+    uint64_t* s_full = b + 2 * TC_NST;
+    uint64_t* p_full = s_full + 2;
+    uint64_t* o_done = s_full + 4;
+    uint64_t* drain = s_full + 6;
+    const uint32_t tg = tbase + g * TC_TMEM_COLS;
+    const uint32_t tO = tg + 128;
+    const int nb = nb_of(g);
     constexpr int fmt = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
     constexpr uint32_t idS = idesc_f16(fmt, 0, TC_KB);
     constexpr uint32_t idPV = idesc_f16(fmt, 1, TC_D);
     const uint32_t q_addr = smem_u32(qs);
+    unsigned char* gst = stages + size_t(g) * TC_NST * TC_STAGE;
     bool dead = !mbar_wait_bounded(q_ready, 0, a.st);
     dead = __any_sync(0xffffffffu, dead);
-    const int lp_blk = (npages - 1) / TC_PPB;  // block holding the sequence's last page
-    for (int j = 0; j <= nblk && !dead; ++j) {
-      if (j < nblk) {
-        const int st = j % TC_NST;
+    const int lp_blk = (npages - 1) / TC_PPB;  // global block holding the sequence's last page
+    for (int j = 0; j <= nb && !dead; ++j) {
+      if (j < nb) {
+        const int st = j % TC_NST, jg = j * NG + g;
         if (!mbar_wait_bounded(&full[st], (j / TC_NST) & 1, a.st)) dead = true;
         dead = __any_sync(0xffffffffu, dead);
         if (dead) break;
-        if (j == lp_blk && lpl < TC_P && npages - 1 < n_pg) {
+        if (jg == lp_blk && lpl < TC_P && npages - 1 < n_pg) {
           // rows lpl..15 of the last page's V slice were never written: zero them
-          uint4* vt = reinterpret_cast<uint4*>(stages + size_t(st) * TC_STAGE + TC_KTILE +
-                                               (npages - 1 - j * TC_PPB) * TC_PAGE);
+          uint4* vt = reinterpret_cast<uint4*>(gst + size_t(st) * TC_STAGE + TC_KTILE +
+                                               (npages - 1 - jg * TC_PPB) * TC_PAGE);
           for (int r = lpl * 8 + lane; r < TC_P * 8; r += 32) vt[r] = make_uint4(0u, 0u, 0u, 0u);
           fence_proxy_async_smem();
           __syncwarp();
         }
         if (lane == 0) {
           tc_fence_after();
-          const uint32_t kaddr = smem_u32(stages + size_t(st) * TC_STAGE);
-          const uint32_t dS = tbase + (j & 1) * TC_KB;
+          const uint32_t kaddr = smem_u32(gst + size_t(st) * TC_STAGE);
+          const uint32_t dS = tg + (j & 1) * TC_KB;
 #pragma unroll
           for (int k = 0; k < TC_D / 16; ++k)
             umma_ss(dS, sw128_desc(q_addr + 32 * k), sw128_desc(kaddr + 32 * k), idS, k > 0);
@@ -406,8 +439,8 @@ __global__ void __launch_bounds__(TC_THREADS, 2) prefill_tc_kernel(const __grid_
         if (dead) break;
         if (lane == 0) {
           tc_fence_after();
-          const uint32_t vaddr = smem_u32(stages + size_t(stp) * TC_STAGE + TC_KTILE);
-          const uint32_t aP = tbase + (jp & 1) * TC_KB;
+          const uint32_t vaddr = smem_u32(gst + size_t(stp) * TC_STAGE + TC_KTILE);
+          const uint32_t aP = tg + (jp & 1) * TC_KB;
 #pragma unroll
           for (int k = 0; k < TC_KB / 16; ++k)
             umma_ts(tO, aP + 8 * k, sw128_desc(vaddr + 16 * 128 * k), idPV, (jp > 0 || k > 0) ? 1u : 0u);
@@ -423,17 +456,26 @@ __global__ void __launch_bounds__(TC_THREADS, 2) prefill_tc_kernel(const __grid_
       mbar_wait_bounded(drain, 0, a.st);
     }
     __syncwarp();
-  } else {
-    // ------------------------------------------------------------ softmax warps
+  } else if (grp >= 0) {
+    // ------------------------------------------------------------ softmax warps of group grp
+    const int g = grp;
+    uint64_t* s_full = gbar(g) + 2 * TC_NST;
+    uint64_t* p_full = s_full + 2;
+    uint64_t* o_done = s_full + 4;
+    const uint32_t tg = tbase + g * TC_TMEM_COLS;
+    const uint32_t tO = tg + 128;
+    const int nb = nb_of(g);
     const int q4 = warp & 3;  // TMEM lane quarter this warp may access
     const int r = r_sm;
     const int jq = jq_sm;
     const bool valid = jq < ql;
     const int lim = valid ? kv - ql + jq : -1;  // last visible key of this row
+    if (g == 0) {
 #pragma unroll
-    for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(qs + r * 128 + ((c ^ (r & 7)) << 4)) = qv[c];
-    fence_proxy_async_smem();
-    mbar_arrive(q_ready);
+      for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(qs + r * 128 + ((c ^ (r & 7)) << 4)) = qv[c];
+      fence_proxy_async_smem();
+      mbar_arrive(q_ready);
+    }
     const uint32_t lane_off = uint32_t(q4 * 32) << 16;
     const float sl2 = a.scale_log2;
     float m = -INFINITY, l = 0.f;
@@ -442,7 +484,7 @@ __global__ void __launch_bounds__(TC_THREADS, 2) prefill_tc_kernel(const __grid_
     // waits for P.V of block j - 2 (its P buffer is about to be overwritten) and,
     // only when it rescales O, for P.V of block j - 1 — so a try_wait on a
     // parity never meets a barrier two phases ahead.
-    for (int j = 0; j < nblk; ++j) {
+    for (int j = 0; j < nb; ++j) {
       const int b = j & 1;
       if (!mbar_wait_bounded(&s_full[b], (j >> 1) & 1, a.st)) dead = true;
       if (j >= 2 && !dead && !mbar_wait_bounded(&o_done[b], ((j - 2) >> 1) & 1, a.st)) dead = true;
@@ -450,8 +492,8 @@ __global__ void __launch_bounds__(TC_THREADS, 2) prefill_tc_kernel(const __grid_
       if (dead) break;
       tc_fence_after();
       uint32_t sr[64];
-      tmem_ld64(tbase + lane_off + b * TC_KB, sr);
-      const int kb0 = j * TC_KB;
+      tmem_ld64(tg + lane_off + b * TC_KB, sr);
+      const int kb0 = (j * NG + g) * TC_KB;
       if (sl2 <= 0.f) {  // a non-positive scale: scale first so the masked -inf stays the minimum
 #pragma unroll
         for (int i = 0; i < 64; ++i) sr[i] = __float_as_uint(__uint_as_float(sr[i]) * sl2);
@@ -512,30 +554,63 @@ __global__ void __launch_bounds__(TC_THREADS, 2) prefill_tc_kernel(const __grid_
       for (int u = 0; u < 4; ++u) f32x2_split(lt2[u], lt[2 * u], lt[2 * u + 1]);
       const float ls = ((lt[0] + lt[1]) + (lt[2] + lt[3])) + ((lt[4] + lt[5]) + (lt[6] + lt[7]));
       l += ls;
-      tmem_st32(tbase + lane_off + b * TC_KB, pk);
+      tmem_st32(tg + lane_off + b * TC_KB, pk);
       tc_fence_before();
       mbar_arrive(&p_full[b]);
     }
-    // epilogue: O / l -> the row in global memory (P.V of the last block done;
-    // the barrier's previous phase was waited at block nblk - 1)
-    if (nblk > 0 && !dead && !mbar_wait_bounded(&o_done[(nblk - 1) & 1], ((nblk - 1) >> 1) & 1, a.st)) dead = true;
+    // epilogue: P.V of the group's last block done (the barrier's previous
+    // phase was waited at block nb - 1)
+    if (nb > 0 && !dead && !mbar_wait_bounded(&o_done[(nb - 1) & 1], ((nb - 1) >> 1) & 1, a.st)) dead = true;
     dead = __any_sync(0xffffffffu, dead);
-    if (!dead && nblk > 0) {
+    if (NG == 2 && g == 1) {
+      // publish this row's (max, sum); O (if the group had blocks) is final
+      s_ml[r] = make_float2(m, l);
+      tc_fence_before();
+      mbar_arrive(b_done);
+    } else if (!dead && nb > 0) {
+      float m1 = -INFINITY, l1 = 0.f;
+      int nb1 = 0;
+      if (NG == 2) {
+        if (!mbar_wait_bounded(b_done, 0, a.st)) dead = true;
+        const float2 ml = s_ml[r];
+        m1 = ml.x;
+        l1 = ml.y;
+        nb1 = nb_of(1);
+      }
+      // merge: both parts to the larger of the two maxima (a part without
+      // visible keys in this row has max -inf and weight 0)
+      const float mm = fmaxf(m, m1);
+      const float w0 = m == -INFINITY ? 0.f : ex2(m - mm);
+      const float w1 = (nb1 == 0 || m1 == -INFINITY) ? 0.f : ex2(m1 - mm);
+      const float lsum = l * w0 + l1 * w1;
+      const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
+      const float f0 = w0 * inv, f1 = w1 * inv;
       tc_fence_after();
-      uint32_t o[2][32];
-      tmem_ld32(tO + lane_off, o[0]);
-      tmem_ld32(tO + lane_off + 32, o[1]);
-      if (T* orow = out_row(r)) {
-        const float inv = l > 0.f ? 1.f / l : 0.f;
+      T* orow = out_row(r);
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          const int e = c * 8;
-          uint4 v;
-          v.x = MmaOp<T>::pack(__uint_as_float(o[e >> 5][e & 31]) * inv, __uint_as_float(o[e >> 5][(e & 31) + 1]) * inv);
-          v.y = MmaOp<T>::pack(__uint_as_float(o[e >> 5][(e & 31) + 2]) * inv, __uint_as_float(o[e >> 5][(e & 31) + 3]) * inv);
-          v.z = MmaOp<T>::pack(__uint_as_float(o[e >> 5][(e & 31) + 4]) * inv, __uint_as_float(o[e >> 5][(e & 31) + 5]) * inv);
-          v.w = MmaOp<T>::pack(__uint_as_float(o[e >> 5][(e & 31) + 6]) * inv, __uint_as_float(o[e >> 5][(e & 31) + 7]) * inv);
-          reinterpret_cast<uint4*>(orow)[c] = v;
+      for (int hf = 0; hf < 2; ++hf) {
+        uint32_t o[32];
+        tmem_ld32(tO + lane_off + hf * 32, o);
+        if (NG == 2 && nb1 > 0) {
+          uint32_t o1[32];
+          tmem_ld32(tbase + TC_TMEM_COLS + 128 + lane_off + hf * 32, o1);
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            o[i] = __float_as_uint(__uint_as_float(o[i]) * f0 + __uint_as_float(o1[i]) * f1);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f0);
+        }
+        if (!dead && orow) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint4 v;
+            v.x = MmaOp<T>::pack(__uint_as_float(o[8 * c]), __uint_as_float(o[8 * c + 1]));
+            v.y = MmaOp<T>::pack(__uint_as_float(o[8 * c + 2]), __uint_as_float(o[8 * c + 3]));
+            v.z = MmaOp<T>::pack(__uint_as_float(o[8 * c + 4]), __uint_as_float(o[8 * c + 5]));
+            v.w = MmaOp<T>::pack(__uint_as_float(o[8 * c + 6]), __uint_as_float(o[8 * c + 7]));
+            reinterpret_cast<uint4*>(orow)[hf * 4 + c] = v;
+          }
         }
       }
     }
@@ -546,12 +621,14 @@ __global__ void __launch_bounds__(TC_THREADS, 2) prefill_tc_kernel(const __grid_
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tbase), "r"(TC_TMEM_COLS)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tbase), "r"(TC_TMEM_COLS * NG)
                  : "memory");
   }
 }
 
-size_t tc_smem() { return 1024 + TC_QTILE + size_t(TC_NST) * TC_STAGE + 256; }
+size_t tc_smem(int ng) {
+  return 1024 + TC_QTILE + size_t(ng) * TC_NST * TC_STAGE + 8 * (ng * (2 * TC_NST + 7) + 2) + 128 * 8;
+}
 
 // 3-D TMA load (the query tile: dims D, query head, token).
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
@@ -1522,6 +1599,19 @@ int prefill_lean_mode() {
   return mode;
 }
 
+// Whether one-CTA-per-tile launches split each tile's key blocks over two
+// groups of the CTA: PKV_PREFILL_SPLIT unset or 1 = launches of at most one CTA
+// per SM, 0 = never, 2 = every such launch (tests).
+int prefill_split_mode() {
+  static const int mode = [] {
+    const char* e = getenv("PKV_PREFILL_SPLIT");
+    if (e && e[0] == '0') return 0;
+    if (e && e[0] == '2') return 2;
+    return 1;
+  }();
+  return mode;
+}
+
 // Tensor map of the step's query rows q [n_tokens][n_heads][64] as dims
 // (D, query head, token): one box = the G heads of one KV head for TPT tokens,
 // landing in shared memory as row = token * G + head, 128B-swizzled (the
@@ -1550,12 +1640,13 @@ int q_tmap(int32_t dtype, const void* q, int n_tokens, int n_heads, int groups, 
 }
 
 
-// Launches one of the three kernels: `qm` == nullptr -> one CTA per (tile, KV
-// head) (prefill_tc_kernel), otherwise a persistent kernel over `grid` CTAs:
-// prefill_tc_lean_kernel when `lean`, else prefill_tc_persistent_kernel.
+// Launches one of the kernels: `qm` == nullptr -> one CTA per (tile, KV
+// head) (prefill_tc_kernel, its key blocks split over `ng` groups), otherwise a
+// persistent kernel over `grid` CTAs: prefill_tc_lean_kernel when `lean`, else
+// prefill_tc_persistent_kernel.
 template <typename T, int G>
-int launch_tc_t(const pkv_pool& p, const CUtensorMap& tm, const CUtensorMap* qm, bool lean, const TcArgs& a,
-                int grid, cudaStream_t s) {
+int launch_tc_t(const pkv_pool& p, const CUtensorMap& tm, const CUtensorMap* qm, bool lean, int ng,
+                const TcArgs& a, int grid, cudaStream_t s) {
   static std::mutex mu;
   static std::vector<char> ready;
   int dev = 0;
@@ -1564,8 +1655,10 @@ int launch_tc_t(const pkv_pool& p, const CUtensorMap& tm, const CUtensorMap* qm,
     std::lock_guard<std::mutex> lock(mu);
     if ((int)ready.size() <= dev) ready.resize(dev + 1, 0);
     if (!ready[dev]) {
-      PKV_CUDA_RET(cudaFuncSetAttribute(prefill_tc_kernel<T, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        int(tc_smem())));
+      PKV_CUDA_RET(cudaFuncSetAttribute(prefill_tc_kernel<T, G, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        int(tc_smem(1))));
+      PKV_CUDA_RET(cudaFuncSetAttribute(prefill_tc_kernel<T, G, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        int(tc_smem(2))));
       PKV_CUDA_RET(cudaFuncSetAttribute(prefill_tc_persistent_kernel<T, G>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, int(tcp_smem())));
       PKV_CUDA_RET(cudaFuncSetAttribute(prefill_tc_lean_kernel<T, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1582,19 +1675,21 @@ int launch_tc_t(const pkv_pool& p, const CUtensorMap& tm, const CUtensorMap* qm,
   else if (qm)
     PKV_CUDA_RET(launch_kernel(prefill_tc_persistent_kernel<T, G>, dim3(grid), dim3(TC_THREADS), tcp_smem(), s,
                                true, tm, *qm, a));
+  else if (ng == 2)
+    PKV_CUDA_RET(launch_kernel(prefill_tc_kernel<T, G, 2>, dim3(grid), dim3(384), tc_smem(2), s, true, tm, a));
   else
-    PKV_CUDA_RET(launch_kernel(prefill_tc_kernel<T, G>, dim3(grid), dim3(TC_THREADS), tc_smem(), s, true, tm, a));
+    PKV_CUDA_RET(launch_kernel(prefill_tc_kernel<T, G, 1>, dim3(grid), dim3(TC_THREADS), tc_smem(1), s, true, tm, a));
   return PKV_OK;
 }
 
 template <typename T>
-int launch_tc_g(const pkv_pool& p, int groups, const CUtensorMap& tm, const CUtensorMap* qm, bool lean,
+int launch_tc_g(const pkv_pool& p, int groups, const CUtensorMap& tm, const CUtensorMap* qm, bool lean, int ng,
                 const TcArgs& a, int grid, cudaStream_t s) {
   switch (groups) {
-    case 1: return launch_tc_t<T, 1>(p, tm, qm, lean, a, grid, s);
-    case 2: return launch_tc_t<T, 2>(p, tm, qm, lean, a, grid, s);
-    case 4: return launch_tc_t<T, 4>(p, tm, qm, lean, a, grid, s);
-    case 8: return launch_tc_t<T, 8>(p, tm, qm, lean, a, grid, s);
+    case 1: return launch_tc_t<T, 1>(p, tm, qm, lean, ng, a, grid, s);
+    case 2: return launch_tc_t<T, 2>(p, tm, qm, lean, ng, a, grid, s);
+    case 4: return launch_tc_t<T, 4>(p, tm, qm, lean, ng, a, grid, s);
+    case 8: return launch_tc_t<T, 8>(p, tm, qm, lean, ng, a, grid, s);
   }
   return fail(PKV_ERR_UNSUPPORTED, "tcgen05 prefill kernel: unsupported GQA group size");
 }
@@ -1649,8 +1744,13 @@ int prefill_tc_attend(const pkv_pool& p, int layer, int n_heads, const void* q, 
     grid = std::min(items, lean ? int64_t(TL_MINB) * num_sms() : slots);
   }
   if (grid > 0x7fffffff) return fail(PKV_ERR_ARG, "prefill batch too large for one launch");
-  if (p.dtype == PKV_F16) return launch_tc_g<__half>(p, groups, tm, qmp, lean, a, int(grid), s);
-  return launch_tc_g<__nv_bfloat16>(p, groups, tm, qmp, lean, a, int(grid), s);
+  // one CTA per tile: a launch of at most one CTA per SM splits each tile's key
+  // blocks over two groups of its CTA (the longest tile's chain is the launch)
+  const int split_mode = prefill_split_mode();
+  const int ng = !qmp && (split_mode == 2 || (split_mode == 1 && items <= num_sms())) ? 2 : 1;
+  if (ng == 2) a.early_ctas = num_sms();  // one CTA per SM
+  if (p.dtype == PKV_F16) return launch_tc_g<__half>(p, groups, tm, qmp, lean, ng, a, int(grid), s);
+  return launch_tc_g<__nv_bfloat16>(p, groups, tm, qmp, lean, ng, a, int(grid), s);
 }
 
 }  // namespace pkv

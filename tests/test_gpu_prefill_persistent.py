@@ -1,5 +1,5 @@
 """
-The three tcgen05 prefill kernels against each other's paths and the oracle.
+The tcgen05 prefill kernels against each other's paths and the oracle.
 
 Launches of more than one wave of CTAs (more than two tiles x KV heads per SM)
 run a persistent kernel — by default the lean one (three CTAs per SM), with
@@ -7,7 +7,9 @@ run a persistent kernel — by default the lean one (three CTAs per SM), with
 tile. The environment variables (read once per process) move the lines:
 ``PKV_PREFILL_PERSISTENT=2`` sends every launch to the two-CTA persistent
 kernel, ``PKV_PREFILL_PERSISTENT=0`` none; ``PKV_PREFILL_LEAN=2`` every launch
-to the lean kernel. Here the whole prefill suite and the reference-scheduler
+to the lean kernel; one-CTA-per-tile launches split each tile's key blocks
+over two groups of the CTA when they have at most one CTA per SM
+(``PKV_PREFILL_SPLIT=2``: every such launch, ``0``: none). Here the whole prefill suite and the reference-scheduler
 trace replay run again in child processes under each setting, so each kernel
 meets every case (chunks after long prefixes, tile and page edges, every GQA
 group size, bf16, NaN-poisoned page tails, radix sharing with copy-on-write,
@@ -42,7 +44,8 @@ ROOT = Path(__file__).resolve().parents[1]
 KERNELS = {
     "persistent": {"PKV_PREFILL_PERSISTENT": "2", "PKV_PREFILL_LEAN": "0"},
     "lean": {"PKV_PREFILL_LEAN": "2"},
-    "per_tile": {"PKV_PREFILL_PERSISTENT": "0", "PKV_PREFILL_LEAN": "0"},
+    "per_tile": {"PKV_PREFILL_PERSISTENT": "0", "PKV_PREFILL_LEAN": "0", "PKV_PREFILL_SPLIT": "0"},
+    "per_tile_split": {"PKV_PREFILL_PERSISTENT": "0", "PKV_PREFILL_LEAN": "0", "PKV_PREFILL_SPLIT": "2"},
 }
 
 
