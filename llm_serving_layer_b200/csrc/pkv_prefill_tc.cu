@@ -356,13 +356,16 @@ __global__ void __launch_bounds__(NG == 1 ? TC_THREADS : 384, NG == 1 ? 2 : 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
-    if (lane == 0) {
+    // lane g < NG loads group g's blocks (global blocks g, g + NG, ...), so a
+    // group that falls behind does not hold up the other's copies
+    if (lane < NG) {
+      const int g = lane;
+      uint64_t* b = gbar(g);
       const int kvc = 2 * a.layer;
-      int issued = 0;
+      int issued = 0;  // local blocks of group g issued
       bool dead = false;
-      for (int j = 0; j < nblk; ++j) {
-        const int g = j % NG, jj = j / NG, st = jj % TC_NST;
-        uint64_t* b = gbar(g);
+      for (int jj = 0; jj * NG + g < nblk; ++jj) {
+        const int j = jj * NG + g, st = jj % TC_NST;
         if (jj >= TC_NST && !mbar_wait_bounded_sleepy(&b[TC_NST + st], ((jj / TC_NST) - 1) & 1, a.st, 64)) {
           dead = true;
           break;
@@ -377,14 +380,11 @@ __global__ void __launch_bounds__(NG == 1 ? TC_THREADS : 384, NG == 1 ? 2 : 1)
           tma_load_4d(kd + u * TC_PAGE, &tmap, &b[st], 0, row, h, kvc);
           tma_load_4d(kd + TC_KTILE + u * TC_PAGE, &tmap, &b[st], 0, row, h, kvc + 1);
         }
-        issued = j + 1;
+        issued = jj + 1;
       }
-      // let this CTA's own copies land before its shared memory can be released
+      // let this group's copies land before the CTA's shared memory can be released
       if (dead)
-        for (int i = max(0, issued - NG * TC_NST); i < issued; ++i) {
-          const int g = i % NG, ii = i / NG;
-          mbar_wait_bounded(&gbar(g)[ii % TC_NST], (ii / TC_NST) & 1, nullptr);
-        }
+        for (int i = max(0, issued - TC_NST); i < issued; ++i) mbar_wait_bounded(&b[i % TC_NST], (i / TC_NST) & 1, nullptr);
     }
   } else if (warp >= 1 && warp <= NG) {
     // ------------------------------------------------------------ MMA issuer of group warp - 1
