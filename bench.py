@@ -1017,7 +1017,8 @@ def run_prefill(torch, bk, args, device) -> dict:
     bk.check_status()
     us = e0.elapsed_time(e1) * 1e3 / reps
     fl, _ = prefill_step_work(None, [s for s, _ in specs], en)
-    batched = {"us_per_launch": round(us, 1), "tflops": round(fl / us / 1e6, 1), "frac": round(fl / us / 1e6 / peak, 4)}
+    batched = {"us_per_launch": round(us, 1), "tflops": round(fl / us / 1e6, 1), "frac": round(fl / us / 1e6 / peak, 4),
+               "kernel": "prefill_tc_lean_kernel (tcgen05; three persistent CTAs per SM)"}
     del qbig
     if work["blocks_used"] > bk.num_blocks:
         return {"skipped": f"pool has {bk.num_blocks} blocks, config 3 needs {work['blocks_used']}",
@@ -1098,7 +1099,9 @@ def run_prefill(torch, bk, args, device) -> dict:
         "prompt_tok_per_s_incl_cached": round(work["prompt_tokens"] / (ms / 1e3), 1),
         "ms_total": round(ms, 3), "attn_ms_total": round(attn_ms, 3),
         "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak, "unit": "TFLOP/s",
-                     "frac": round(achieved / peak, 4), "peak_kind": peak_kind, "kernel": "prefill_kernel",
+                     "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                     "kernel": "prefill_tc_kernel (tcgen05; one CTA per tile, key blocks split over two groups of the "
+                               "CTA in launches of at most one CTA per SM)",
                      "avg_launch_us": round(attn_ms * 1e3 / (len(graphs) * L), 2),
                      "timing": "CUDA events around each step's 16 back-to-back attend launches"},
         "batched_64x512": batched,
