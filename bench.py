@@ -716,6 +716,12 @@ def run_b200(args) -> None:
         dist.destroy_process_group()
 
 
+# Layers of the next e2e step issued before the host waits for this step's
+# outputs (measured on one B200, 200 steps: 0 -> 0.706 ms per step, 8 -> 0.676,
+# 12 -> 0.640-0.646, all 16 -> 0.642; 2 and 4 were slower, 1.0-1.05 ms)
+E2E_AHEAD = 12
+
+
 def run_e2e(torch, bk, tables, ctx, args, device, ws, dist, n_graphs, meta_mode="device",
             fused=False) -> dict:
     """Public-API end to end: per step, the step's BatchMeta (``meta_mode``
@@ -731,9 +737,11 @@ def run_e2e(torch, bk, tables, ctx, args, device, ws, dist, n_graphs, meta_mode=
     buffer while step s computes, and the outputs (written by attend into one
     buffer, out=) leave four layers at a time as soon as those layers finished.
     The next step's meta is built and planned on the host while this step's GPU
-    work runs. Every step's inputs and outputs cross the link inside the timed
-    region (the first timed step also copies its own). Timed with CUDA events
-    around the whole loop."""
+    work runs, and its first E2E_AHEAD layers are issued before the host waits
+    for this step's outputs. Every step's inputs and outputs cross the link
+    inside the timed region (the first timed step also copies its own; the host
+    reads every step's outputs before the next step's remaining layers are
+    issued). Timed with CUDA events around the whole loop."""
     from llm_serving_layer_b200 import DeviceBlockTables
     from llm_serving_layer_b200.meta import build_meta
 
@@ -794,16 +802,23 @@ def run_e2e(torch, bk, tables, ctx, args, device, ws, dist, n_graphs, meta_mode=
             ev_ready[b].record(cstream)
         staged.add(step)
 
-    def one(s):
-        # step s runs with the meta built during step s - 1; the next step's meta
-        # is built on the host while this step's GPU work runs (one build per step)
-        m = nxt.pop(s) if s in nxt else meta_for_step(s)
-        if s not in staged:
-            h2d(s)
-        staged.discard(s)
+    # the previous step's outputs of group g have left dout (recorded on the output stream)
+    ev_gcopy = [torch.cuda.Event() for _ in range(L // GROUP)]
+    for e in ev_gcopy:
+        e.record(comp)
+    issued = {}  # step -> layers already issued
+    stop_at = [0]  # no step at or past this one is issued ahead
+    # with the host assembler the per-field copies of the next meta queue behind
+    # the layers issued ahead (measured slower: 275 k -> 234 k tok/s): none there
+    ahead = E2E_AHEAD if meta_mode == "device" else 0
+
+    def issue_layers(s, m, lo, hi):
         b = s % 2
-        comp.wait_event(ev_ready[b])
-        for layer in range(L):
+        if lo == 0:
+            comp.wait_event(ev_ready[b])
+        for layer in range(lo, hi):
+            if layer % GROUP == 0:
+                comp.wait_event(ev_gcopy[layer // GROUP])
             if fused:
                 bk.append_attend(layer, dk[b][layer], dv[b][layer], dq[b][layer], SCALE, m, out=dout[layer])
             else:
@@ -815,6 +830,17 @@ def run_e2e(torch, bk, tables, ctx, args, device, ws, dist, n_graphs, meta_mode=
                 h2d(s + 1)
             if layer % GROUP == GROUP - 1:
                 ev_out[layer].record(comp)
+        issued[s] = hi
+
+    def one(s):
+        # step s runs with the meta built during step s - 1; the next step's meta
+        # is built on the host while this step's GPU work runs (one build per step)
+        m = nxt.pop(s) if s in nxt else meta_for_step(s)
+        if s not in staged:
+            h2d(s)
+        staged.discard(s)
+        b = s % 2
+        issue_layers(s, m, issued.pop(s, 0), L)
         ev_free[b].record(comp)
         # each group of layers' outputs leaves as soon as the group is done (the
         # output stream waits for its event); issued together to switch streams once
@@ -822,19 +848,29 @@ def run_e2e(torch, bk, tables, ctx, args, device, ws, dist, n_graphs, meta_mode=
             for g0 in range(0, L, GROUP):
                 ostream.wait_event(ev_out[g0 + GROUP - 1])
                 hout[g0:g0 + GROUP].copy_(dout[g0:g0 + GROUP], non_blocking=True)
+                ev_gcopy[g0 // GROUP].record(ostream)
         nxt[s + 1] = meta_for_step(s + 1)
         # plan the next step now (B200PagedBackend.plan): its host work and plan
         # kernel run while this step's GPU work drains, not before its first layer
         bk.plan(nxt[s + 1])
+        if ahead and s + 1 < stop_at[0]:
+            # the next step's first E2E_AHEAD layers queue behind this step on the
+            # GPU while the host waits for this step's outputs: the GPU does not
+            # idle through the last output copy and the host's wake-up (each of
+            # those layers waits for its output group's previous copy)
+            issue_layers(s + 1, nxt[s + 1], 0, ahead)
         ostream.synchronize()
 
     if meta_mode == "device":  # admission: each row gets the blocks of its history
         for r in range(N_SEQ):
             bt.bind(r, tables[r][:(int(ctx[r]) + base + P - 1) // P])
+    stop_at[0] = 3
     for s in range(3):
         one(s)
     nxt.clear()
     staged.clear()
+    issued.clear()
+    stop_at[0] = steps
     torch.cuda.synchronize()
     nxt[0] = meta_for_step(0)
     meta_in.update(bytes=0, n=0)
@@ -858,7 +894,9 @@ def run_e2e(torch, bk, tables, ctx, args, device, ws, dist, n_graphs, meta_mode=
                "host build_meta (one copy per BatchMeta field)")
             + " built per step (the next step's while this one runs), inputs one copy per step (one step "
               "ahead, double-buffered), outputs into one buffer (attend out=) copied back 4 layers at a time, "
-              "on two side streams")
+              "on two side streams"
+            + (f"; the next step's first {E2E_AHEAD} layers issued before waiting for this step's outputs"
+               if meta_mode == "device" else ""))
     return {"value": round(N_SEQ * ws * steps / (ms / 1e3), 1), "unit": UNIT, "h2d_bytes_per_step": int(h2d_bytes),
             "d2h_bytes_per_step": int(d2h), "steps": steps, "ms_per_step": round(ms / steps, 4), "path": path}
 
