@@ -832,10 +832,13 @@ def run_e2e(torch, bk, tables, ctx, args, device, ws, dist, n_graphs, meta_mode=
                 ev_out[layer].record(comp)
         issued[s] = hi
 
+    last = [None]  # (step, BatchMeta) of the latest step
+
     def one(s):
         # step s runs with the meta built during step s - 1; the next step's meta
         # is built on the host while this step's GPU work runs (one build per step)
         m = nxt.pop(s) if s in nxt else meta_for_step(s)
+        last[0] = (s, m)
         if s not in staged:
             h2d(s)
         staged.discard(s)
@@ -885,6 +888,14 @@ def run_e2e(torch, bk, tables, ctx, args, device, ws, dist, n_graphs, meta_mode=
     torch.cuda.synchronize()
     ms = max_over_ranks(dist, e0.elapsed_time(e1), device)
     bk.check_status()
+    # the outputs that reached the host are the attention of their step: the last
+    # step's last layer, recomputed through the same call, must equal them bit for bit
+    s_last, m_last = last[0]
+    b = s_last % 2
+    # (append_kv / append_attend already wrote the step's rows: attend alone recomputes it)
+    ref = bk.attend(dq[b][L - 1], L - 1, SCALE, m_last)
+    torch.cuda.synchronize()
+    outputs_ok = bool(torch.equal(ref.cpu(), hout[L - 1]))
     h2d_bytes = hx.numel() * 2 + meta_in["bytes"] // max(meta_in["n"], 1)
     d2h = hout.numel() * 2
     path = (("B200PagedBackend.append_attend per layer" if fused else "B200PagedBackend.append_kv/attend per layer")
@@ -898,7 +909,8 @@ def run_e2e(torch, bk, tables, ctx, args, device, ws, dist, n_graphs, meta_mode=
             + (f"; the next step's first {E2E_AHEAD} layers issued before waiting for this step's outputs"
                if meta_mode == "device" else ""))
     return {"value": round(N_SEQ * ws * steps / (ms / 1e3), 1), "unit": UNIT, "h2d_bytes_per_step": int(h2d_bytes),
-            "d2h_bytes_per_step": int(d2h), "steps": steps, "ms_per_step": round(ms / steps, 4), "path": path}
+            "d2h_bytes_per_step": int(d2h), "steps": steps, "ms_per_step": round(ms / steps, 4),
+            "outputs_equal_recomputed_last_layer": outputs_ok, "path": path}
 
 
 def prefill_workload(seed: int):
