@@ -717,8 +717,11 @@ def run_b200(args) -> None:
 
 
 # Layers of the next e2e step issued before the host waits for this step's
-# outputs (measured on one B200, 200 steps: 0 -> 0.706 ms per step, 8 -> 0.676,
-# 12 -> 0.640-0.646, all 16 -> 0.642; 2 and 4 were slower, 1.0-1.05 ms)
+# outputs (measured on one B200, 200 steps: 0 -> 0.706 ms per step, 12 ->
+# 0.641-0.645 over repeated runs). The input copy of the step after that is
+# issued only once the host has waited: issued with the early layers it started
+# beside this step's last output copy and runs fell into a slow mode (0.86-1.05
+# ms per step) at random.
 E2E_AHEAD = 12
 
 
@@ -824,10 +827,6 @@ def run_e2e(torch, bk, tables, ctx, args, device, ws, dist, n_graphs, meta_mode=
             else:
                 bk.append_kv(layer, dk[b][layer], dv[b][layer], m)
                 bk.attend(dq[b][layer], layer, SCALE, m, out=dout[layer])
-            if layer == 0:
-                # the next step's inputs travel while this step computes; issued
-                # after the first layer's launches so that those are not delayed
-                h2d(s + 1)
             if layer % GROUP == GROUP - 1:
                 ev_out[layer].record(comp)
         issued[s] = hi
@@ -843,7 +842,14 @@ def run_e2e(torch, bk, tables, ctx, args, device, ws, dist, n_graphs, meta_mode=
             h2d(s)
         staged.discard(s)
         b = s % 2
-        issue_layers(s, m, issued.pop(s, 0), L)
+        lo = issued.pop(s, 0)
+        issue_layers(s, m, lo, lo + 1)
+        # the next step's inputs travel while this step computes; issued after
+        # the first layer this call issues (so that its launches are not
+        # delayed) and after the wait for the previous step's outputs (so that
+        # the copy does not start beside that step's last output copy)
+        h2d(s + 1)
+        issue_layers(s, m, lo + 1, L)
         ev_free[b].record(comp)
         # each group of layers' outputs leaves as soon as the group is done (the
         # output stream waits for its event); issued together to switch streams once
