@@ -717,12 +717,12 @@ def run_b200(args) -> None:
 
 
 # Layers of the next e2e step issued before the host waits for this step's
-# outputs (measured on one B200, 200 steps: 0 -> 0.706 ms per step, 12 ->
-# 0.641-0.645 over repeated runs). The input copy of the step after that is
-# issued only once the host has waited: issued with the early layers it started
-# beside this step's last output copy and runs fell into a slow mode (0.86-1.05
-# ms per step) at random.
-E2E_AHEAD = 12
+# outputs (measured on one B200, 200 steps, pairs of runs: 0 -> 0.706 ms per
+# step, 8 -> 0.673, 12 -> 0.648-0.686, all 16 -> 0.646-0.647). The input copy of
+# the step after that is issued only once the host has waited: issued with the
+# early layers it started beside this step's last output copy and runs fell
+# into a slow mode (0.86-1.05 ms per step) at random.
+E2E_AHEAD = 16
 
 
 def run_e2e(torch, bk, tables, ctx, args, device, ws, dist, n_graphs, meta_mode="device",
@@ -817,7 +817,7 @@ def run_e2e(torch, bk, tables, ctx, args, device, ws, dist, n_graphs, meta_mode=
 
     def issue_layers(s, m, lo, hi):
         b = s % 2
-        if lo == 0:
+        if lo == 0 and hi > 0:
             comp.wait_event(ev_ready[b])
         for layer in range(lo, hi):
             if layer % GROUP == 0:
@@ -843,13 +843,13 @@ def run_e2e(torch, bk, tables, ctx, args, device, ws, dist, n_graphs, meta_mode=
         staged.discard(s)
         b = s % 2
         lo = issued.pop(s, 0)
-        issue_layers(s, m, lo, lo + 1)
+        issue_layers(s, m, lo, min(lo + 1, L))
         # the next step's inputs travel while this step computes; issued after
         # the first layer this call issues (so that its launches are not
         # delayed) and after the wait for the previous step's outputs (so that
         # the copy does not start beside that step's last output copy)
         h2d(s + 1)
-        issue_layers(s, m, lo + 1, L)
+        issue_layers(s, m, min(lo + 1, L), L)
         ev_free[b].record(comp)
         # each group of layers' outputs leaves as soon as the group is done (the
         # output stream waits for its event); issued together to switch streams once
