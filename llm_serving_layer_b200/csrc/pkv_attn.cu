@@ -480,6 +480,25 @@ __global__ void __maxnreg__(DK_MAXNREG) decode_kernel(const __grid_constant__ CU
       tma_prefetch_l2_4d(&tmap, 0, id * DK_P, 0, kv_coord + 1);
     }
   }
+  // The producer also loads the ring's first stages now, up to the first page
+  // that is the last page of its sequence: the kernels allowed to run ahead
+  // of this one (the append, the RoPE rotation, attention launches) write the
+  // pool only at the step's new rows, which lie in the sequences' last pages.
+  int pre = 0;
+  if (warp == n_cons) {
+    if (lane == 0) {
+      for (int i = 0; i < min(R, NST); ++i) {
+        const int4 d = __ldcg(a.desc + pos(i));
+        if ((d.y >> 5) & 1) break;
+        unsigned char* dst = stages + size_t(i) * STAGE;
+        mbar_arrive_expect_tx(&full[i], 2u * n_cons * DK_P * DK_D * 2);
+        tma_load_4d(dst, &tmap, &full[i], 0, d.x * DK_P, 0, kv_coord);
+        tma_load_4d(dst + PAGE, &tmap, &full[i], 0, d.x * DK_P, 0, kv_coord + 1);
+        pre = i + 1;
+      }
+    }
+    pre = __shfl_sync(0xffffffffu, pre, 0);
+  }
   pdl_wait();  // q, this step's appended rows and the split-K counters are written by earlier kernels
   // page descriptors: lane j holds window entries [wb + j] (cur) and [wb + 32 + j] (nxt)
   int wb = 0;
@@ -557,7 +576,7 @@ __global__ void __maxnreg__(DK_MAXNREG) decode_kernel(const __grid_constant__ CU
   if (warp == n_cons) {
     // ---------------- producer warp
     bool dead = false;
-    for (int i = 0; i < R; ++i) {
+    for (int i = pre; i < R; ++i) {
       slide_to(i);
       const int4 d = desc_at(i);
       const int st = i % NST;
