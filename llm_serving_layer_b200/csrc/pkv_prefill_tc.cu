@@ -3,19 +3,25 @@
 // memory (TMEM), operands staged in shared memory by TMA.
 //
 // Work item = one tile of query rows of one sequence for ONE KV head: 128 rows =
-// TPT = 128 / G tokens x the G query heads that share the KV head. Two kernels
+// TPT = 128 / G tokens x the G query heads that share the KV head. The kernels
 // share the roles and the per-block arithmetic:
 //   prefill_tc_kernel             one CTA per item (launches of at most one
 //                                 wave: 2 CTAs per SM); row r = head * TPT +
 //                                 token; the softmax threads load the query rows.
-//   prefill_tc_persistent_kernel  at most 2 CTAs per SM, each walking its share
-//                                 of the items (larger launches): TMEM and
+//                                 In launches of at most one CTA per SM its
+//                                 key blocks are split over two groups of the
+//                                 CTA (NG = 2), merged in the epilogue.
+//   prefill_tc_lean_kernel        larger launches: 3 persistent CTAs per SM
+//                                 claiming items, 128 TMEM columns each, P in
+//                                 shared memory (described at the kernel).
+//   prefill_tc_persistent_kernel  (PKV_PREFILL_LEAN=0) at most 2 CTAs per SM,
+//                                 each walking its share of the items: TMEM and
 //                                 barriers are set up once, the producer loads
 //                                 each item's query tile by TMA into a double
 //                                 buffer (row r = token * G + head) ahead of its
 //                                 K/V blocks, and O is double-buffered in TMEM so
 //                                 one item's epilogue overlaps the next item's MMAs.
-// Warp roles:
+// Warp roles (prefill_tc_kernel with NG = 1 and the two-CTA persistent kernel):
 //   warp 0      TMA producer: one 2 KiB box per page per K and V (that head's
 //               [16 tok][64] slice), 4 pages = one 64-key block per stage,
 //               4 stages; pages past the tile's last visible key read the
