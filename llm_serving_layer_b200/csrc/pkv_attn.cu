@@ -480,6 +480,20 @@ __global__ void __maxnreg__(DK_MAXNREG) decode_kernel(const __grid_constant__ CU
       tma_prefetch_l2_4d(&tmap, 0, id * DK_P, 0, kv_coord + 1);
     }
   }
+  // The consumer threads warm L2 with the query rows of the range's first
+  // sequences (the tail piece's first, then from the head): a hint, so it may
+  // run before the wait (the loads after it read through L2, where a later
+  // write by an earlier kernel lands too). One 128-byte row per head.
+  if (warp < n_cons && sf >= 0 && sl >= sf) {
+    const int tid = warp * 32 + lane, k = tid / a.n_heads, hh = tid % a.n_heads;
+    const int sq = k == 0 ? sl : sf + k - 1;
+    if (sq <= sl && sq < a.n_seqs) {
+      const int row = a.rows ? __ldcg(a.rows + sq) : sq;
+      if (row >= 0 && row < a.n_rows)
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(static_cast<const T*>(a.q) +
+                                                       (int64_t(row) * a.n_heads + hh) * DK_D));
+    }
+  }
   // The producer also loads the ring's first stages now, up to the first page
   // that is the last page of its sequence: the kernels allowed to run ahead
   // of this one (the append, the RoPE rotation, attention launches) write the
